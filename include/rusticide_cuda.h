@@ -1,0 +1,254 @@
+/*
+ * rusticide_cuda.h -- C ABI of the B200 token-sampling engine.
+ *
+ * The engine is a batched, device-resident drop-in for the sampler of the Rust
+ * crate rusticide-sampling (platform-cortex/rusticide,
+ * crates/rusticide-sampling). Each row of an R x V row-major f32 logit matrix
+ * is one independent call of the reference's Sampler, with the same result
+ * bit for bit given the same uniform draw.
+ *
+ * Conventions
+ *  - Plain C: no exceptions, no C++ or torch types cross this boundary.
+ *  - Pointers named d_* are device pointers of the sampler's device; h_* are
+ *    host pointers. Logits are borrowed and never written.
+ *  - Calls are asynchronous on `stream` (a cudaStream_t passed as void*; NULL
+ *    is the legacy default stream) unless documented otherwise. The return
+ *    value reports argument and launch errors only; per-row outcomes land in
+ *    the caller's d_out_status array (rsc_row_status).
+ *  - One rsc_sampler per host thread or stream: a handle owns scratch memory
+ *    that concurrent calls would share.
+ *  - No call traps, asserts or waits without bound on the device.
+ */
+#ifndef RUSTICIDE_CUDA_H
+#define RUSTICIDE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RSC_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define RSC_API __attribute__((visibility("default")))
+#else
+#define RSC_API
+#endif
+
+/* Call-level status. */
+typedef enum {
+    RSC_OK = 0,
+    RSC_ERR_INVALID_ARGUMENT = 1, /* null pointer where one is required, bad flag */
+    RSC_ERR_INVALID_SHAPE = 2,    /* rows/vocab/stride inconsistent (SamplingError::InvalidShape) */
+    RSC_ERR_VOCAB_TOO_LARGE = 3,  /* vocab >= 2^31 (SamplingError::VocabOverflow class) */
+    RSC_ERR_CAPACITY = 4,         /* rows or vocab above what the handle was created for */
+    RSC_ERR_CUDA = 5,             /* a CUDA runtime call or kernel launch failed */
+    RSC_ERR_NOT_INITIALIZED = 6,  /* null or destroyed handle */
+    RSC_ERR_NO_DEVICE = 7
+} rsc_status;
+
+/* Per-row outcome written to d_out_status (int32 per row).
+ * The low byte is the result; higher bits are informational flags. */
+enum {
+    RSC_ROW_OK = 0,               /* d_out_ids[row] holds the token */
+    RSC_ROW_NO_VALID_TOKENS = 1,  /* SamplingError::NoValidTokens, src/error.rs:11-12 */
+    RSC_ROW_VOCAB_OVERFLOW = 2,   /* SamplingError::VocabOverflow, src/error.rs:13-14 */
+    RSC_ROW_INTERNAL = 3,         /* a bounded device wait gave up; row not sampled */
+    RSC_ROW_FLAG_DRAW_NEAR_BOUNDARY = 1 << 8, /* |u - CDF edge| < 1e-6 at the chosen token */
+    RSC_ROW_FLAG_LARGE_PATH = 1 << 9          /* the row took the large-survivor-set kernel */
+};
+
+/* SamplingParams, crates/rusticide-sampling/src/params.rs:5-12. One set per
+ * call; repetition_penalty is carried for layout parity and is not applied by
+ * rsc_sample (the reference's sample_logits does not apply it either). */
+typedef struct {
+    float temperature;
+    uint32_t top_k;
+    float top_p;
+    float repetition_penalty;
+    uint64_t seed;
+} rsc_params;
+
+typedef struct rsc_sampler rsc_sampler;
+
+/* Human-readable name of a call-level status (static storage). */
+RSC_API const char *rsc_status_string(rsc_status status);
+
+/* ABI version of the loaded library (RSC_ABI_VERSION at build time). */
+RSC_API int rsc_abi_version(void);
+
+/*
+ * Creates a sampler on `device` for batches of up to max_rows rows of up to
+ * max_vocab logits. Allocates its scratch memory here, once; the sampling
+ * calls allocate nothing. Replaces `Sampler::new(seed)`
+ * (crates/rusticide-sampling/src/sampler.rs:17-23) for a batch: per-row
+ * generator states are the caller's d_rng_states array (rsc_rng_seed).
+ */
+RSC_API rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab,
+                              rsc_sampler **out);
+RSC_API rsc_status rsc_sampler_destroy(rsc_sampler *sampler);
+
+/*
+ * Batched Sampler::sample_logits (src/sampler.rs:44-54): per row, NaN -> -inf,
+ * scale by 1/T (T > 0), keep the top_k largest with every tie of the k-th
+ * (src/candidates.rs:24-53), then the top_p nucleus (src/candidates.rs:55-78),
+ * softmax (src/filters.rs:5-15), then argmax when T == 0 or top_k == 1, else an
+ * inverse-CDF draw (src/sampler.rs:111-121).
+ *
+ * d_logits    rows x vocab f32, row r at d_logits + r * row_stride (row_stride >= vocab).
+ * d_uniforms  per-row uniform in [0,1) for the draw (device), or NULL.
+ * d_rng_states per-row generator state (device, updated in place) used when
+ *             d_uniforms is NULL; a row's state advances only when the row
+ *             consumed a draw, as the reference's rng does.
+ *             One of d_uniforms / d_rng_states must be non-NULL unless every
+ *             row takes the argmax branch (T == 0 or top_k == 1).
+ * d_out_ids   uint32 per row; d_out_status int32 per row (rsc_row_status);
+ * d_out_probs float per row, nullable: the softmax probability of the chosen
+ *             survivor.
+ */
+RSC_API rsc_status rsc_sample(rsc_sampler *sampler, const float *d_logits, size_t rows,
+                      size_t vocab, size_t row_stride, const rsc_params *params,
+                      const float *d_uniforms, uint64_t *d_rng_states,
+                      uint32_t *d_out_ids, int32_t *d_out_status,
+                      float *d_out_probs, void *stream);
+
+/*
+ * Optional outputs of rsc_sample_ex: the candidate set that survived top-k and
+ * top-p (the reference's Candidates after Candidates::filter,
+ * src/candidates.rs:16-22), per row, in index order.
+ * d_n_survivors   uint32 per row, nullable: size of the set.
+ * d_survivor_ids  rows x survivor_cap uint32, nullable: the first
+ *                 min(n, survivor_cap) token ids of the set.
+ */
+typedef struct {
+    uint32_t *d_n_survivors;
+    uint32_t *d_survivor_ids;
+    size_t survivor_cap;
+} rsc_sample_extras;
+
+/* rsc_sample with optional extra outputs (extras may be NULL). */
+RSC_API rsc_status rsc_sample_ex(rsc_sampler *sampler, const float *d_logits, size_t rows,
+                                 size_t vocab, size_t row_stride, const rsc_params *params,
+                                 const float *d_uniforms, uint64_t *d_rng_states,
+                                 uint32_t *d_out_ids, int32_t *d_out_status,
+                                 float *d_out_probs, const rsc_sample_extras *extras,
+                                 void *stream);
+
+/*
+ * Batched Sampler::greedy_logits (src/sampler.rs:75-88): index of the largest
+ * logit with NaN read as -inf, the LAST one on a tie under f32::total_cmp;
+ * RSC_ROW_NO_VALID_TOKENS when no logit is finite.
+ */
+RSC_API rsc_status rsc_greedy(rsc_sampler *sampler, const float *d_logits, size_t rows,
+                      size_t vocab, size_t row_stride, uint32_t *d_out_ids,
+                      int32_t *d_out_status, void *stream);
+
+/*
+ * Batched Sampler::sample_with_temp after extract_logits (src/sampler.rs:97-105,
+ * src/logits.rs:9-23): temperature == 0 is greedy; otherwise every logit is
+ * multiplied by 1/temperature and the draw runs over the whole row.
+ */
+RSC_API rsc_status rsc_sample_with_temp(rsc_sampler *sampler, const float *d_logits,
+                                size_t rows, size_t vocab, size_t row_stride,
+                                float temperature, const float *d_uniforms,
+                                uint64_t *d_rng_states, uint32_t *d_out_ids,
+                                int32_t *d_out_status, float *d_out_probs,
+                                void *stream);
+
+/*
+ * rusticide_model::generate::pick (crates/rusticide-model/src/generate.rs:117-124):
+ * temperature == 0 routes to rsc_greedy, anything else to rsc_sample.
+ */
+RSC_API rsc_status rsc_pick(rsc_sampler *sampler, const float *d_logits, size_t rows,
+                    size_t vocab, size_t row_stride, const rsc_params *params,
+                    const float *d_uniforms, uint64_t *d_rng_states,
+                    uint32_t *d_out_ids, int32_t *d_out_status,
+                    float *d_out_probs, void *stream);
+
+/*
+ * Host-buffer form of rsc_pick for callers whose logits live in host memory,
+ * as the reference's Model::forward returns them
+ * (crates/rusticide-model/src/model.rs:17): copies h_logits (rows x vocab,
+ * dense) and h_uniforms to the device, samples, and copies ids and statuses
+ * back. Synchronous: returns after h_out_* are written. Host buffers may be
+ * pageable or pinned (pinned is faster). h_uniforms may be NULL when every
+ * row takes the argmax branch.
+ */
+RSC_API rsc_status rsc_pick_host(rsc_sampler *sampler, const float *h_logits,
+                         size_t rows, size_t vocab, const rsc_params *params,
+                         const float *h_uniforms, uint32_t *h_out_ids,
+                         int32_t *h_out_status, float *h_out_probs);
+
+/*
+ * Sampler::penalize / apply_repetition_penalty (src/sampler.rs:107-109,
+ * src/filters.rs:24-35) on device rows: for each listed token inside the
+ * vocabulary, a positive logit is divided by `penalty`, any other multiplied.
+ * d_tokens holds n_tokens uint32 ids applied to every row. In place.
+ */
+RSC_API rsc_status rsc_penalize(rsc_sampler *sampler, float *d_logits, size_t rows,
+                        size_t vocab, size_t row_stride,
+                        const uint32_t *d_tokens, size_t n_tokens,
+                        float penalty, void *stream);
+
+/*
+ * Seeds per-row generator states: state[r] = seeds[r] (device arrays), the
+ * wyrand stream that fastrand::Rng::with_seed starts from
+ * (src/sampler.rs:17-23). The stream's f32 conversion is restated from the
+ * published generator and is unverified against fastrand 2.5.0 output.
+ */
+RSC_API rsc_status rsc_rng_seed(const uint64_t *d_seeds, uint64_t *d_rng_states,
+                        size_t rows, void *stream);
+
+/*
+ * Vocab-sharded sampling, step 1 of 2 (no reference counterpart: the reference
+ * samples a whole row on one CPU thread). Each rank holds columns
+ * [shard_offset, shard_offset + shard_vocab) of every row. Writes one
+ * fixed-size record per row to d_records (rsc_shard_record_bytes(top_k) bytes
+ * each): the shard's scaled row maximum, the count of its logits that are not
+ * -inf, and every logit that can survive the global top-k (at most
+ * top_k + RSC_SHARD_TIE_CAP of them, with an overflow count). The caller
+ * all-gathers the records of all ranks (NCCL over NVLink) into a
+ * [n_shards][rows] array and calls rsc_shard_merge.
+ */
+#define RSC_SHARD_TIE_CAP 24
+RSC_API size_t rsc_shard_record_bytes(uint32_t top_k);
+RSC_API rsc_status rsc_shard_partial(rsc_sampler *sampler, const float *d_logits,
+                             size_t rows, size_t shard_vocab, size_t row_stride,
+                             size_t shard_offset, size_t global_vocab,
+                             const rsc_params *params, void *d_records,
+                             void *stream);
+
+/*
+ * Vocab-sharded sampling, step 2 of 2: merges the gathered records
+ * ([n_shards][rows] records, shard-major) into the same per-row result as
+ * rsc_sample on the unsharded row. Every rank that calls it with the same
+ * gathered records and uniforms computes identical outputs. Rows whose shards
+ * overflowed their record report RSC_ROW_INTERNAL and must be resampled
+ * unsharded.
+ */
+RSC_API rsc_status rsc_shard_merge(rsc_sampler *sampler, const void *d_records,
+                           size_t n_shards, size_t rows, size_t global_vocab,
+                           const rsc_params *params, const float *d_uniforms,
+                           uint64_t *d_rng_states, uint32_t *d_out_ids,
+                           int32_t *d_out_status, float *d_out_probs,
+                           void *stream);
+
+/*
+ * Evaluates the library's binary32 exp, the function the sampler applies to
+ * v - max (Rust's f32::exp, i.e. glibc expf, src/filters.rs:7 and
+ * src/candidates.rs:64), on n device floats: d_y[i] = exp(d_x[i]). Exposed so
+ * that callers can verify it against their platform's expf. Asynchronous.
+ */
+RSC_API rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream);
+
+/* Number of kernel launches the library issued since the handle was created
+ * (for the benchmark's launch count). */
+RSC_API uint64_t rsc_launch_count(const rsc_sampler *sampler);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RUSTICIDE_CUDA_H */

@@ -1,0 +1,402 @@
+// C ABI of the sampling engine (include/rusticide_cuda.h): argument checks,
+// routing between the kernels, and the handle that owns scratch memory.
+//
+// Routing of rsc_sample (Sampler::sample_logits):
+//  - scale finite and > 0, and top-k on or vocab <= kSmallCap: the streaming
+//    top-k kernel; rows whose survivors overflow its shared-memory list are
+//    appended to a device list that the large-survivor kernel, launched right
+//    after on the same stream, drains (no host round trip);
+//  - otherwise every row goes to the large-survivor kernel.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "rsc_kernels.h"
+
+struct rsc_sampler {
+    int device = -1;
+    size_t max_rows = 0;
+    size_t max_vocab = 0;
+    int num_sms = 0;
+    uint32_t large_slots = 0;
+    uint32_t *large_rows = nullptr;   // [max_rows]
+    uint32_t *large_count = nullptr;  // [1]
+    uint32_t *scratch = nullptr;      // [large_slots][4 * max_vocab]
+    // Device staging of rsc_pick_host.
+    float *stage_logits = nullptr;
+    float *stage_uniforms = nullptr;
+    uint32_t *stage_ids = nullptr;
+    int32_t *stage_status = nullptr;
+    float *stage_probs = nullptr;
+    cudaStream_t host_stream = nullptr;
+    uint64_t launches = 0;
+    bool alive = false;
+};
+
+namespace {
+
+constexpr size_t kMaxVocab = (size_t{1} << 31) - 1;
+
+rsc_status cuda_status(cudaError_t e) { return e == cudaSuccess ? RSC_OK : RSC_ERR_CUDA; }
+
+// Makes `device` current for the duration of a call and restores the caller's.
+class DeviceGuard {
+  public:
+    explicit DeviceGuard(int device) {
+        cudaGetDevice(&prev_);
+        if (prev_ != device) cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (cur != prev_ && prev_ >= 0) cudaSetDevice(prev_);
+    }
+
+  private:
+    int prev_ = -1;
+};
+
+rsc_status check_shape(const rsc_sampler *s, const void *logits, size_t rows, size_t vocab,
+                       size_t row_stride) {
+    if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
+    if (vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (rows > 0 && vocab > 0 && row_stride < vocab) return RSC_ERR_INVALID_SHAPE;
+    if (rows > s->max_rows || vocab > s->max_vocab) return RSC_ERR_CAPACITY;
+    if (rows > 0 && vocab > 0 && !logits) return RSC_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(logits) & 3u) != 0) return RSC_ERR_INVALID_ARGUMENT;
+    return RSC_OK;
+}
+
+rsc::CallParams make_params(const rsc_params &p, size_t vocab, const float *uniforms,
+                            uint64_t *rng_states) {
+    rsc::CallParams cp;
+    cp.temperature = p.temperature;
+    // candidates.rs:25-29: 1/T for T > 0, else 1.
+    cp.scale = p.temperature > 0.0f ? 1.0f / p.temperature : 1.0f;
+    cp.top_k = p.top_k;
+    cp.top_p = p.top_p;
+    cp.topk_active = p.top_k != 0 && static_cast<size_t>(p.top_k) < vocab;
+    cp.topp_active = p.top_p < 1.0f;
+    cp.argmax_branch = p.temperature == 0.0f || p.top_k == 1;
+    cp.normal_scale = std::isfinite(cp.scale) && cp.scale > 0.0f;
+    cp.mode = rsc::kModeSampleLogits;
+    cp.uniforms = uniforms;
+    cp.rng_states = rng_states;
+    cp.out_nsurv = nullptr;
+    cp.out_surv = nullptr;
+    cp.surv_cap = 0;
+    return cp;
+}
+
+rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t vocab,
+                       size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
+                       int32_t *status, float *probs, cudaStream_t stream) {
+    if (rows == 0) return RSC_OK;
+    const uint32_t v = static_cast<uint32_t>(vocab);
+    const bool small = cp.mode == rsc::kModeSampleLogits && cp.normal_scale &&
+                       (cp.topk_active || vocab <= rsc::kSmallCap);
+    cudaError_t e;
+    if (small) {
+        e = cudaMemsetAsync(s->large_count, 0, sizeof(uint32_t), stream);
+        if (e != cudaSuccess) return RSC_ERR_CUDA;
+        e = rsc::launch_stream_topk(logits, rows, v, row_stride, cp, ids, status, probs,
+                                    s->large_rows, s->large_count, s->num_sms, stream);
+        ++s->launches;
+        if (e != cudaSuccess) return RSC_ERR_CUDA;
+        e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->large_rows,
+                              s->large_count, s->scratch, s->large_slots, stream);
+        ++s->launches;
+        return cuda_status(e);
+    }
+    e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, nullptr, nullptr,
+                          s->scratch, s->large_slots, stream);
+    ++s->launches;
+    return cuda_status(e);
+}
+
+rsc_status greedy_impl(rsc_sampler *s, const float *logits, size_t rows, size_t vocab,
+                       size_t row_stride, uint32_t *ids, int32_t *status, cudaStream_t stream) {
+    // Grid rows are limited to 65535 per launch.
+    for (size_t r0 = 0; r0 < rows; r0 += 65535) {
+        size_t nr = rows - r0 < 65535 ? rows - r0 : 65535;
+        cudaError_t e = rsc::launch_greedy(logits + r0 * row_stride, nr,
+                                           static_cast<uint32_t>(vocab), row_stride, ids + r0,
+                                           status + r0, s->num_sms, stream);
+        ++s->launches;
+        if (e != cudaSuccess) return RSC_ERR_CUDA;
+    }
+    return RSC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *rsc_status_string(rsc_status status) {
+    switch (status) {
+        case RSC_OK: return "ok";
+        case RSC_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case RSC_ERR_INVALID_SHAPE: return "invalid shape";
+        case RSC_ERR_VOCAB_TOO_LARGE: return "vocabulary too large";
+        case RSC_ERR_CAPACITY: return "batch above the sampler's capacity";
+        case RSC_ERR_CUDA: return "CUDA error";
+        case RSC_ERR_NOT_INITIALIZED: return "sampler not initialized";
+        case RSC_ERR_NO_DEVICE: return "no CUDA device";
+    }
+    return "unknown status";
+}
+
+int rsc_abi_version(void) { return RSC_ABI_VERSION; }
+
+rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab, rsc_sampler **out) {
+    if (!out) return RSC_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (max_vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return RSC_ERR_NO_DEVICE;
+    if (device < 0 || device >= ndev) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(device);
+    rsc_sampler *s = new (std::nothrow) rsc_sampler();
+    if (!s) return RSC_ERR_INVALID_ARGUMENT;
+    s->device = device;
+    s->max_rows = max_rows < 1 ? 1 : max_rows;
+    s->max_vocab = max_vocab < 1 ? 1 : max_vocab;
+    cudaError_t e = cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, device);
+    // One large-survivor CTA per SM, at most one per row.
+    size_t slots = static_cast<size_t>(s->num_sms);
+    if (slots > s->max_rows) slots = s->max_rows;
+    s->large_slots = static_cast<uint32_t>(slots);
+    if (e == cudaSuccess) e = cudaMalloc(&s->large_rows, s->max_rows * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->large_count, sizeof(uint32_t));
+    if (e == cudaSuccess)
+        e = cudaMalloc(&s->scratch, static_cast<size_t>(s->large_slots) * 4u * s->max_vocab *
+                                        sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->stage_logits, s->max_rows * s->max_vocab * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s->stage_uniforms, s->max_rows * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s->stage_ids, s->max_rows * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->stage_status, s->max_rows * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->stage_probs, s->max_rows * sizeof(float));
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->host_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        s->alive = true;
+        rsc_sampler_destroy(s);
+        return RSC_ERR_CUDA;
+    }
+    s->alive = true;
+    *out = s;
+    return RSC_OK;
+}
+
+rsc_status rsc_sampler_destroy(rsc_sampler *s) {
+    if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
+    DeviceGuard guard(s->device);
+    cudaFree(s->large_rows);
+    cudaFree(s->large_count);
+    cudaFree(s->scratch);
+    cudaFree(s->stage_logits);
+    cudaFree(s->stage_uniforms);
+    cudaFree(s->stage_ids);
+    cudaFree(s->stage_status);
+    cudaFree(s->stage_probs);
+    if (s->host_stream) cudaStreamDestroy(s->host_stream);
+    s->alive = false;
+    delete s;
+    return RSC_OK;
+}
+
+rsc_status rsc_sample_ex(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,
+                         size_t row_stride, const rsc_params *params, const float *d_uniforms,
+                         uint64_t *d_rng_states, uint32_t *d_out_ids, int32_t *d_out_status,
+                         float *d_out_probs, const rsc_sample_extras *extras, void *stream) {
+    rsc_status st = check_shape(s, d_logits, rows, vocab, row_stride);
+    if (st != RSC_OK) return st;
+    if (!params || (rows > 0 && (!d_out_ids || !d_out_status))) return RSC_ERR_INVALID_ARGUMENT;
+    rsc::CallParams cp = make_params(*params, vocab, d_uniforms, d_rng_states);
+    if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    if (extras) {
+        if (extras->d_survivor_ids && (extras->survivor_cap == 0 || extras->survivor_cap > 0xffffffffull))
+            return RSC_ERR_INVALID_ARGUMENT;
+        cp.out_nsurv = extras->d_n_survivors;
+        cp.out_surv = extras->d_survivor_ids;
+        cp.surv_cap = static_cast<uint32_t>(extras->survivor_cap);
+    }
+    DeviceGuard guard(s->device);
+    return sample_impl(s, d_logits, rows, vocab, row_stride, cp, d_out_ids, d_out_status,
+                       d_out_probs, static_cast<cudaStream_t>(stream));
+}
+
+rsc_status rsc_sample(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,
+                      size_t row_stride, const rsc_params *params, const float *d_uniforms,
+                      uint64_t *d_rng_states, uint32_t *d_out_ids, int32_t *d_out_status,
+                      float *d_out_probs, void *stream) {
+    return rsc_sample_ex(s, d_logits, rows, vocab, row_stride, params, d_uniforms, d_rng_states,
+                         d_out_ids, d_out_status, d_out_probs, nullptr, stream);
+}
+
+rsc_status rsc_greedy(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,
+                      size_t row_stride, uint32_t *d_out_ids, int32_t *d_out_status,
+                      void *stream) {
+    rsc_status st = check_shape(s, d_logits, rows, vocab, row_stride);
+    if (st != RSC_OK) return st;
+    if (rows > 0 && (!d_out_ids || !d_out_status)) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    return greedy_impl(s, d_logits, rows, vocab, row_stride, d_out_ids, d_out_status,
+                       static_cast<cudaStream_t>(stream));
+}
+
+rsc_status rsc_sample_with_temp(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,
+                                size_t row_stride, float temperature, const float *d_uniforms,
+                                uint64_t *d_rng_states, uint32_t *d_out_ids,
+                                int32_t *d_out_status, float *d_out_probs, void *stream) {
+    rsc_status st = check_shape(s, d_logits, rows, vocab, row_stride);
+    if (st != RSC_OK) return st;
+    if (rows > 0 && (!d_out_ids || !d_out_status)) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    if (temperature == 0.0f)  // sampler.rs:98-100
+        return greedy_impl(s, d_logits, rows, vocab, row_stride, d_out_ids, d_out_status, cs);
+    if (rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    rsc_params p{temperature, 0u, 1.0f, 1.0f, 0u};
+    rsc::CallParams cp = make_params(p, vocab, d_uniforms, d_rng_states);
+    cp.mode = rsc::kModeSampleWithTemp;
+    cp.scale = 1.0f / temperature;  // apply_temperature, filters.rs:17-22
+    cp.topk_active = false;
+    cp.topp_active = false;
+    cp.argmax_branch = false;
+    return sample_impl(s, d_logits, rows, vocab, row_stride, cp, d_out_ids, d_out_status,
+                       d_out_probs, cs);
+}
+
+rsc_status rsc_pick(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,
+                    size_t row_stride, const rsc_params *params, const float *d_uniforms,
+                    uint64_t *d_rng_states, uint32_t *d_out_ids, int32_t *d_out_status,
+                    float *d_out_probs, void *stream) {
+    if (!params) return RSC_ERR_INVALID_ARGUMENT;
+    if (params->temperature == 0.0f) {
+        rsc_status st = rsc_greedy(s, d_logits, rows, vocab, row_stride, d_out_ids, d_out_status, stream);
+        if (st == RSC_OK && d_out_probs && rows > 0) {
+            // greedy_logits computes no probability.
+            DeviceGuard guard(s->device);
+            cudaError_t e = cudaMemsetAsync(d_out_probs, 0xff, rows * sizeof(float),
+                                            static_cast<cudaStream_t>(stream));
+            if (e != cudaSuccess) return RSC_ERR_CUDA;
+        }
+        return st;
+    }
+    return rsc_sample(s, d_logits, rows, vocab, row_stride, params, d_uniforms, d_rng_states,
+                      d_out_ids, d_out_status, d_out_probs, stream);
+}
+
+rsc_status rsc_pick_host(rsc_sampler *s, const float *h_logits, size_t rows, size_t vocab,
+                         const rsc_params *params, const float *h_uniforms, uint32_t *h_out_ids,
+                         int32_t *h_out_status, float *h_out_probs) {
+    rsc_status st = check_shape(s, h_logits, rows, vocab, vocab);
+    if (st != RSC_OK) return st;
+    if (!params || (rows > 0 && (!h_out_ids || !h_out_status))) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows == 0) return RSC_OK;
+    const bool argmax = params->temperature == 0.0f || params->top_k == 1;
+    if (!argmax && !h_uniforms) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    cudaStream_t cs = s->host_stream;
+    cudaError_t e = cudaMemcpyAsync(s->stage_logits, h_logits, rows * vocab * sizeof(float),
+                                    cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess && h_uniforms)
+        e = cudaMemcpyAsync(s->stage_uniforms, h_uniforms, rows * sizeof(float),
+                            cudaMemcpyHostToDevice, cs);
+    if (e != cudaSuccess) return RSC_ERR_CUDA;
+    st = rsc_pick(s, s->stage_logits, rows, vocab, vocab, params,
+                  h_uniforms ? s->stage_uniforms : nullptr, nullptr, s->stage_ids,
+                  s->stage_status, h_out_probs ? s->stage_probs : nullptr, cs);
+    if (st != RSC_OK) return st;
+    e = cudaMemcpyAsync(h_out_ids, s->stage_ids, rows * sizeof(uint32_t), cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(h_out_status, s->stage_status, rows * sizeof(int32_t),
+                            cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess && h_out_probs)
+        e = cudaMemcpyAsync(h_out_probs, s->stage_probs, rows * sizeof(float),
+                            cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
+    return cuda_status(e);
+}
+
+rsc_status rsc_penalize(rsc_sampler *s, float *d_logits, size_t rows, size_t vocab,
+                        size_t row_stride, const uint32_t *d_tokens, size_t n_tokens,
+                        float penalty, void *stream) {
+    rsc_status st = check_shape(s, d_logits, rows, vocab, row_stride);
+    if (st != RSC_OK) return st;
+    if (n_tokens > 0 && !d_tokens) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows == 0 || n_tokens == 0) return RSC_OK;
+    DeviceGuard guard(s->device);
+    cudaError_t e = rsc::launch_penalize(d_logits, rows, static_cast<uint32_t>(vocab), row_stride,
+                                         d_tokens, n_tokens, penalty,
+                                         static_cast<cudaStream_t>(stream));
+    ++s->launches;
+    return cuda_status(e);
+}
+
+rsc_status rsc_rng_seed(const uint64_t *d_seeds, uint64_t *d_rng_states, size_t rows, void *stream) {
+    if (rows == 0) return RSC_OK;
+    if (!d_seeds || !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    return cuda_status(rsc::launch_rng_seed(d_seeds, d_rng_states, rows,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+size_t rsc_shard_record_bytes(uint32_t top_k) { return rsc::shard_record_bytes(top_k); }
+
+rsc_status rsc_shard_partial(rsc_sampler *s, const float *d_logits, size_t rows,
+                             size_t shard_vocab, size_t row_stride, size_t shard_offset,
+                             size_t global_vocab, const rsc_params *params, void *d_records,
+                             void *stream) {
+    rsc_status st = check_shape(s, d_logits, rows, shard_vocab, row_stride);
+    if (st != RSC_OK) return st;
+    if (!params || (rows > 0 && !d_records)) return RSC_ERR_INVALID_ARGUMENT;
+    if (global_vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (shard_offset + shard_vocab > global_vocab) return RSC_ERR_INVALID_SHAPE;
+    rsc::CallParams cp = make_params(*params, global_vocab, nullptr, nullptr);
+    // Only a row whose top-k is on can be reduced to a small record, and the
+    // streaming kernel needs a scale that creates no NaN.
+    if (!cp.topk_active || !cp.normal_scale) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows == 0) return RSC_OK;
+    DeviceGuard guard(s->device);
+    cudaError_t e = rsc::launch_shard_partial(
+        d_logits, rows, static_cast<uint32_t>(shard_vocab), row_stride,
+        static_cast<uint32_t>(shard_offset), cp, d_records, rsc::shard_record_bytes(params->top_k),
+        s->num_sms, static_cast<cudaStream_t>(stream));
+    ++s->launches;
+    return cuda_status(e);
+}
+
+rsc_status rsc_shard_merge(rsc_sampler *s, const void *d_records, size_t n_shards, size_t rows,
+                           size_t global_vocab, const rsc_params *params, const float *d_uniforms,
+                           uint64_t *d_rng_states, uint32_t *d_out_ids, int32_t *d_out_status,
+                           float *d_out_probs, void *stream) {
+    if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
+    if (!params || n_shards == 0) return RSC_ERR_INVALID_ARGUMENT;
+    if (global_vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (rows > s->max_rows) return RSC_ERR_CAPACITY;
+    if (rows > 0 && (!d_records || !d_out_ids || !d_out_status)) return RSC_ERR_INVALID_ARGUMENT;
+    rsc::CallParams cp = make_params(*params, global_vocab, d_uniforms, d_rng_states);
+    if (!cp.topk_active || !cp.normal_scale) return RSC_ERR_INVALID_ARGUMENT;
+    if (n_shards * (static_cast<size_t>(params->top_k) + RSC_SHARD_TIE_CAP) > rsc::kSmallCap)
+        return RSC_ERR_CAPACITY;
+    if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows == 0) return RSC_OK;
+    DeviceGuard guard(s->device);
+    cudaError_t e = rsc::launch_shard_merge(d_records, n_shards, rows,
+                                            rsc::shard_record_bytes(params->top_k), cp, d_out_ids,
+                                            d_out_status, d_out_probs, s->num_sms,
+                                            static_cast<cudaStream_t>(stream));
+    ++s->launches;
+    return cuda_status(e);
+}
+
+rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream) {
+    if (n == 0) return RSC_OK;
+    if (!d_x || !d_y) return RSC_ERR_INVALID_ARGUMENT;
+    return cuda_status(rsc::launch_expf(d_x, d_y, n, static_cast<cudaStream_t>(stream)));
+}
+
+uint64_t rsc_launch_count(const rsc_sampler *s) { return s && s->alive ? s->launches : 0; }
+
+}  // extern "C"

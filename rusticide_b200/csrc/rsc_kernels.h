@@ -1,0 +1,79 @@
+// Internal launch interface between the C ABI (api.cu) and the kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "rsc_common.cuh"
+
+namespace rsc {
+
+// Survivor sets up to this size are finished in shared memory by the
+// streaming kernel; larger ones (top-k disabled on a wide row, or ties)
+// go to the large-survivor kernel.
+constexpr uint32_t kSmallCap = 4096;
+
+cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
+                          uint32_t *out_ids, int32_t *out_status, int num_sms,
+                          cudaStream_t stream);
+
+// Streaming top-k kernel for rows whose survivors fit kSmallCap. Rows that
+// overflow are appended to large_rows[*large_count].
+cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
+                               size_t row_stride, const CallParams &p, uint32_t *out_ids,
+                               int32_t *out_status, float *out_probs, uint32_t *large_rows,
+                               uint32_t *large_count, int num_sms, cudaStream_t stream);
+
+// Large-survivor kernel. With large_rows == nullptr it processes rows
+// [0, rows); otherwise the rows listed in large_rows[0 .. *large_count).
+// Scratch: `slots` regions of 4 * vocab uint32 each.
+cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
+                         const CallParams &p, uint32_t *out_ids, int32_t *out_status,
+                         float *out_probs, const uint32_t *large_rows,
+                         const uint32_t *large_count, uint32_t *scratch, uint32_t slots,
+                         cudaStream_t stream);
+
+// Vocab-sharded record: this header, then uint32 key[k + RSC_SHARD_TIE_CAP]
+// and uint32 index[k + RSC_SHARD_TIE_CAP] (global indices), entries sorted by
+// (key desc, index asc). Keys are f32::total_cmp keys of the scaled logits.
+struct ShardRecordHeader {
+    float max_scaled;    // max of the shard's scaled logits (f32::max fold)
+    float sum_exp;       // sum of exp(v - max_scaled) over the shard (fast exp; diagnostic)
+    uint32_t n_finite;   // logits that are not -inf
+    uint32_t n_cand;     // entries that follow
+    uint32_t n_dropped;  // entries at or above the local threshold that did not fit
+    uint32_t last_key;   // key of the last entry
+    uint32_t flags;      // 0 ok; 1 candidate list overflow; 2 a device wait gave up
+    uint32_t reserved;
+};
+static_assert(sizeof(ShardRecordHeader) == 32, "record header layout");
+
+inline size_t shard_record_bytes(uint32_t top_k) {
+    size_t entries = static_cast<size_t>(top_k) + RSC_SHARD_TIE_CAP;
+    size_t b = sizeof(ShardRecordHeader) + 8 * entries;
+    return (b + 15) & ~static_cast<size_t>(15);
+}
+
+cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shard_vocab,
+                                 size_t row_stride, uint32_t shard_offset, const CallParams &p,
+                                 void *records, size_t rec_bytes, int num_sms,
+                                 cudaStream_t stream);
+
+cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows, size_t rec_bytes,
+                               const CallParams &p, uint32_t *out_ids, int32_t *out_status,
+                               float *out_probs, int num_sms, cudaStream_t stream);
+
+cudaError_t launch_penalize(float *logits, size_t rows, uint32_t vocab, size_t row_stride,
+                            const uint32_t *tokens, size_t n_tokens, float penalty,
+                            cudaStream_t stream);
+
+cudaError_t launch_expf(const float *x, float *y, size_t n, cudaStream_t stream);
+
+cudaError_t launch_rng_seed(const uint64_t *seeds, uint64_t *states, size_t rows,
+                            cudaStream_t stream);
+
+// Shared-memory bytes of the streaming kernel (for occupancy queries).
+size_t stream_topk_smem_bytes();
+
+}  // namespace rsc
