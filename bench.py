@@ -210,6 +210,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows per GPU (default: the config's); for small profiling captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -241,7 +243,7 @@ def main() -> None:
             dist.barrier(device_ids=[local])
 
     params = SamplingParams(cfg.temperature, cfg.top_k, cfg.top_p)
-    rows, vocab = cfg.rows, cfg.vocab
+    rows, vocab = (args.rows or cfg.rows), cfg.vocab
     x, u = device_logits(cfg, rows, 1234 + 7919 * rank, device)
     eng = engine(local)
     eng.ensure(rows, vocab)
