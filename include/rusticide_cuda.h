@@ -236,6 +236,37 @@ RSC_API rsc_status rsc_shard_merge(rsc_sampler *sampler, const void *d_records,
                            void *stream);
 
 /*
+ * Allocation-free form of rsc_sample. It has no counterpart in the reference,
+ * whose sampler runs on the host.
+ *
+ * It is meant for callers that cannot let a library allocate device memory.
+ * One example is a server that reserves almost all of HBM for its KV cache at
+ * start-up, so a later cudaMalloc fails. Another is a runtime that owns
+ * device memory through its own pool. A third is a plugin that has no place
+ * to free a handle. The function takes no rsc_sampler: it samples on the
+ * calling thread's current device, with the same results as rsc_sample, and
+ * calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * Its sorting scratch is a fixed array of RSC_NOALLOC_SCRATCH_BYTES inside the
+ * library's device image. Every GPU that loads the library holds that array
+ * until the process exits. vocab above RSC_NOALLOC_MAX_VOCAB returns
+ * RSC_ERR_CAPACITY. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress). Make that first call before any stream capture.
+ * All calls on a device share the array. Calls whose kernels overlap on the
+ * GPU (different streams with no ordering between them) race on it, so order
+ * them on one stream or with events. Rows are sampled by the large-survivor
+ * kernel, at most RSC_NOALLOC_SCRATCH_BYTES / (16 * vocab) rows at a time, so
+ * it is slower than rsc_sample on the streaming top-k path.
+ */
+#define RSC_NOALLOC_SCRATCH_BYTES (64u << 20)
+#define RSC_NOALLOC_MAX_VOCAB (RSC_NOALLOC_SCRATCH_BYTES / 16u)
+RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t rows, size_t vocab,
+                                      size_t row_stride, const rsc_params *params,
+                                      const float *d_uniforms, uint64_t *d_rng_states,
+                                      uint32_t *d_out_ids, int32_t *d_out_status,
+                                      float *d_out_probs, void *stream);
+
+/*
  * Evaluates the library's binary32 exp, the function the sampler applies to
  * v - max (Rust's f32::exp, i.e. glibc expf, src/filters.rs:7 and
  * src/candidates.rs:64), on n device floats: d_y[i] = exp(d_x[i]). Exposed so

@@ -31,6 +31,8 @@ RSC_ROW_FLAG_DRAW_NEAR_BOUNDARY = 1 << 8
 RSC_ROW_FLAG_LARGE_PATH = 1 << 9
 
 RSC_SHARD_TIE_CAP = 24
+RSC_NOALLOC_SCRATCH_BYTES = 64 << 20
+RSC_NOALLOC_MAX_VOCAB = RSC_NOALLOC_SCRATCH_BYTES // 16
 
 
 class RscParams(ctypes.Structure):
@@ -76,6 +78,8 @@ SIGNATURES = {
     "rsc_shard_record_bytes": (_SZ, [ctypes.c_uint32]),
     "rsc_shard_partial": (_ST, [_P, _P, _SZ, _SZ, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P]),
     "rsc_shard_merge": (_ST, [_P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P, _P]),
+    "rsc_sample_noalloc": (_ST, [_P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P,
+                                 _P]),
     "rsc_expf": (_ST, [_P, _P, _SZ, _P]),
     "rsc_launch_count": (ctypes.c_uint64, [_P]),
 }
