@@ -95,7 +95,8 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
     if (rows == 0) return RSC_OK;
     const uint32_t v = static_cast<uint32_t>(vocab);
     const bool small = cp.mode == rsc::kModeSampleLogits && cp.normal_scale &&
-                       (cp.topk_active || vocab <= rsc::kSmallCap);
+                       ((cp.topk_active && cp.top_k <= rsc::kSmallTopK) ||
+                        (!cp.topk_active && vocab <= rsc::kSmallCap));
     cudaError_t e;
     if (small) {
         e = cudaMemsetAsync(s->large_count, 0, sizeof(uint32_t), stream);
@@ -356,7 +357,8 @@ rsc_status rsc_shard_partial(rsc_sampler *s, const float *d_logits, size_t rows,
     rsc::CallParams cp = make_params(*params, global_vocab, nullptr, nullptr);
     // Only a row whose top-k is on can be reduced to a small record, and the
     // streaming kernel needs a scale that creates no NaN.
-    if (!cp.topk_active || !cp.normal_scale) return RSC_ERR_INVALID_ARGUMENT;
+    if (!cp.topk_active || !cp.normal_scale || params->top_k > rsc::kSmallTopK)
+        return RSC_ERR_INVALID_ARGUMENT;
     if (rows == 0) return RSC_OK;
     DeviceGuard guard(s->device);
     cudaError_t e = rsc::launch_shard_partial(

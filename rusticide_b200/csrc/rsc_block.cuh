@@ -112,15 +112,35 @@ __device__ __forceinline__ uint32_t block_exclusive_add(uint32_t v, uint32_t *re
 }
 
 // ---------------------------------------------------------------------------
-// Bitonic sort, ascending, of n64 (a power of two) 64-bit items in shared
-// memory by the whole block.
+// Synchronisation of a group of threads that runs a collective routine: the
+// whole block, the first NT threads through named barrier BAR, or one warp.
+// A group's threads are threadIdx.x % THREADS = 0 .. THREADS-1 of warps that
+// all belong to it.
 // ---------------------------------------------------------------------------
-template <int THREADS>
-__device__ void block_bitonic_sort(unsigned long long *a, uint32_t n64) {
+struct SyncBlock {
+    __device__ __forceinline__ static void sync() { __syncthreads(); }
+};
+struct SyncWarp {
+    __device__ __forceinline__ static void sync() { __syncwarp(); }
+};
+template <int BAR, int NT>
+struct SyncNamed {
+    __device__ __forceinline__ static void sync() {
+        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Bitonic sort, ascending, of n64 (a power of two) 64-bit items in shared
+// memory by a group of THREADS threads.
+// ---------------------------------------------------------------------------
+template <int THREADS, typename Sync = SyncBlock>
+__device__ void group_bitonic_sort(unsigned long long *a, uint32_t n64) {
+    const uint32_t tid = threadIdx.x % THREADS;
     for (uint32_t k = 2; k <= n64; k <<= 1) {
         for (uint32_t j = k >> 1; j > 0; j >>= 1) {
-            __syncthreads();
-            for (uint32_t t = threadIdx.x; t < n64 / 2; t += THREADS) {
+            Sync::sync();
+            for (uint32_t t = tid; t < n64 / 2; t += THREADS) {
                 uint32_t i = 2 * t - (t & (j - 1));  // lower element of the pair
                 uint32_t l = i + j;
                 bool up = (i & k) == 0;
@@ -132,29 +152,47 @@ __device__ void block_bitonic_sort(unsigned long long *a, uint32_t n64) {
             }
         }
     }
-    __syncthreads();
+    Sync::sync();
+}
+
+template <int THREADS>
+__device__ void block_bitonic_sort(unsigned long long *a, uint32_t n64) {
+    group_bitonic_sort<THREADS, SyncBlock>(a, n64);
 }
 
 // ---------------------------------------------------------------------------
 // Radix select of the k-th largest 32-bit key (1 <= k <= count) among
 // `count` keys produced by get(i). 8-bit digits from the top; `hist` is 256
-// shared counters, `sel` two shared words. All threads return the key.
+// shared counters, `sel` two shared words. Every thread of the group returns
+// the key.
 // ---------------------------------------------------------------------------
-template <int THREADS, typename Get>
-__device__ uint32_t block_select_kth_largest(uint32_t count, uint32_t k, Get get, uint32_t *hist,
+template <int THREADS, typename Sync, typename Get>
+__device__ uint32_t group_select_kth_largest(uint32_t count, uint32_t k, Get get, uint32_t *hist,
                                              uint32_t *sel) {
+    const uint32_t tid = threadIdx.x % THREADS;
     uint32_t prefix = 0, mask = 0;
     uint32_t kk = k;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int b = threadIdx.x; b < 256; b += THREADS) hist[b] = 0;
-        __syncthreads();
-        for (uint32_t i = threadIdx.x; i < count; i += THREADS) {
-            uint32_t key = get(i);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        for (uint32_t b = tid; b < 256; b += THREADS) hist[b] = 0;
+        Sync::sync();
+        // Lanes of a warp that share a digit add once, through their leader:
+        // keys of one row crowd into few top digits, and same-address shared
+        // atomics would serialise.
+        const uint32_t rounds = (count + THREADS - 1) / THREADS;
+        for (uint32_t r = 0; r < rounds; ++r) {
+            const uint32_t i = r * THREADS + tid;
+            uint32_t digit = 256u;
+            if (i < count) {
+                const uint32_t key = get(i);
+                if ((key & mask) == prefix) digit = (key >> shift) & 255u;
+            }
+            const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+            if (digit < 256u && (threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1))
+                atomicAdd(&hist[digit], static_cast<uint32_t>(__popc(peers)));
         }
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            const int lane = threadIdx.x;
+        Sync::sync();
+        if (tid < 32) {
+            const int lane = static_cast<int>(tid);
             // Lane l owns digits 255-8l .. 248-8l (descending).
             uint32_t c[8], tot = 0;
 #pragma unroll
@@ -182,13 +220,19 @@ __device__ uint32_t block_select_kth_largest(uint32_t count, uint32_t k, Get get
                 }
             }
         }
-        __syncthreads();
+        Sync::sync();
         prefix |= sel[0] << shift;
         mask |= 255u << shift;
         kk = sel[1];
-        __syncthreads();
+        Sync::sync();
     }
     return prefix;
+}
+
+template <int THREADS, typename Get>
+__device__ uint32_t block_select_kth_largest(uint32_t count, uint32_t k, Get get, uint32_t *hist,
+                                             uint32_t *sel) {
+    return group_select_kth_largest<THREADS, SyncBlock>(count, k, get, hist, sel);
 }
 
 // ---------------------------------------------------------------------------

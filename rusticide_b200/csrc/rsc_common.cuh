@@ -249,13 +249,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
 }
 
 // Returns true once phase `parity` of the barrier has completed; false if it
-// has not after kWaitLimitNs.
+// has not after kWaitLimitNs. The timer is read once per 256 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     const uint32_t addr = smem_addr(bar);
     if (mbar_try(addr, parity)) return true;
     const unsigned long long t0 = global_ns();
     while (true) {
-        if (mbar_try(addr, parity)) return true;
+#pragma unroll 1
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try(addr, parity)) return true;
         if (global_ns() - t0 > kWaitLimitNs) return false;
     }
 }

@@ -12,7 +12,9 @@ namespace rsc {
 // Survivor sets up to this size are finished in shared memory by the
 // streaming kernel; larger ones (top-k disabled on a wide row, or ties)
 // go to the large-survivor kernel.
-constexpr uint32_t kSmallCap = 4096;
+constexpr uint32_t kSmallCap = 1024;
+// Largest top_k the streaming kernel takes; larger k go to the large kernel.
+constexpr uint32_t kSmallTopK = kSmallCap / 4;
 
 cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                           uint32_t *out_ids, int32_t *out_status, int num_sms,

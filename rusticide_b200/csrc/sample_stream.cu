@@ -2,24 +2,33 @@
 // (crates/rusticide-sampling/src/sampler.rs:44-54) for rows whose surviving
 // candidate set is small, which is every row once top-k is on.
 //
-// One HBM pass per row. A CTA owns a sequence of rows; one thread keeps a ring
-// of NSTAGE shared-memory stages filled with 1-D TMA bulk copies (no
-// multicast) of CHUNK logits, running ahead across row boundaries. Every
-// thread scales its logits (candidates.rs:30-37), turns them into
-// f32::total_cmp keys, and compares them with a running lower bound `tau` of
-// the row's k-th largest key; the rare logits at or above it are appended to a
-// shared candidate list. When the list fills up, a radix select of its k-th
-// largest key raises tau and the list is compacted. The list always holds
-// every logit that can survive top-k, so at the end of the row one more
-// select gives the exact threshold of kth_largest (candidates.rs:93-97).
+// One HBM pass per row, one CTA per SM, three warp roles:
 //
-// The survivors (at most kSmallCap) are then finished in shared memory with
-// the reference's exact arithmetic: top-p over the (value desc, index asc)
-// order with sequential sums (candidates.rs:55-78), softmax in index order
-// (filters.rs:5-15), and the argmax or the inverse-CDF draw
-// (sampler.rs:48-52,111-121). The sequential sums run on one thread: the
-// sets are small, and replaying the reference's order is what makes every
-// result bit-identical.
+//  producer (1 warp, one lane): keeps a ring of kStages shared-memory stages
+//    filled with 1-D TMA bulk copies (no multicast) of kChunk logits, running
+//    ahead across rows; a stage is refilled as soon as the consumers release it.
+//  consumers (8 warps): scale every logit (candidates.rs:30-37) with one
+//    multiply and compare it with a running lower bound `tau` of the row's
+//    k-th largest scaled value; the few logits at or above it are appended to
+//    the row's candidate list. tau comes from per-lane running maxima: each
+//    warp's t-th largest lane maximum (t = ceil(k/8)) stands for t distinct
+//    logits at or above it, so the minimum over the 8 warps is at most the
+//    k-th largest of the row. Every logit that can survive top-k is therefore
+//    in the list. The list is double-buffered per row.
+//  finisher (1 warp): takes a finished list and applies the reference's exact
+//    arithmetic while the consumers stream the next row: the k-th largest key
+//    (candidates.rs:38-43, 93-97), the keep test (:44-51), top-p over the
+//    (value desc, index asc) order with its sequential sums (:55-78), softmax
+//    in index order (filters.rs:5-15), and the argmax or the inverse-CDF draw
+//    (sampler.rs:48-52, 111-121). Sets are small; the sequential sums run on
+//    one lane in the reference's order, so every result is bit-identical.
+//
+// Rows whose list overflows kCap (thousands of logits tied with the k-th) are
+// handed to the large-survivor kernel through a device list.
+//
+// All waits are bounded (mbar_wait); the consumer warps decide together
+// through barrier reductions, so a timeout can never leave some of them at a
+// barrier the others have left.
 #include "rsc_block.cuh"
 #include "rsc_kernels.h"
 
@@ -27,36 +36,55 @@ namespace rsc {
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr uint32_t kChunk = 2048;   // logits per stage (8 KiB)
-constexpr uint32_t kStages = 6;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kFinisherWarp = kConsumerWarps + 1;
+constexpr int kThreads = (kConsumerWarps + 2) * 32;
+constexpr uint32_t kChunk = 4096;     // logits per stage (16 KiB)
+constexpr uint32_t kStages = 8;       // 128 KiB of copies in flight per SM
 constexpr uint32_t kCap = kSmallCap;  // candidate list capacity
-static_assert(kCap >= 2 * kChunk, "a chunk must fit after a compaction");
+constexpr uint32_t kCompactAt = kCap / 2;
+constexpr int kBarConsumers = 1;      // named barrier of the consumer warps
+constexpr uint32_t kRefresh = 4;      // chunks between bound refreshes (and consumer barriers)
+static_assert(kSmallTopK <= 8 * 32, "tau uses the t-th of 32 lane maxima per warp, t = ceil(k/8)");
+static_assert(kSmallTopK <= kCompactAt / 2, "the list must hold k plus a chunk's new candidates");
+
+using ConsumerSync = SyncNamed<kBarConsumers, kConsumers>;
+
+struct CandList {
+    uint32_t key[kCap];
+    uint32_t idx[kCap];
+};
+
+// Workspace of one finishing warp.
+struct FinishWork {
+    unsigned long long items[kCap];
+    float vals[kCap];
+    uint32_t hist[256];
+    uint32_t sel[2];
+};
 
 struct StreamSmem {
     alignas(128) float ring[kStages][kChunk];
-    alignas(16) union {
-        struct {
-            uint32_t key[kCap];
-            uint32_t idx[kCap];
-        } cand;
-        unsigned long long items[kCap];
-    } u;
-    alignas(16) float vals[kCap];
+    CandList list[2];
+    FinishWork fw;
     double exp_tab[32];
     uint64_t full[kStages];
-    uint32_t hist[256];
-    uint32_t sel[2];
-    uint32_t count;
-    uint32_t overflow;
+    uint64_t empty[kStages];
+    uint64_t list_full[2];
+    uint64_t list_empty[2];
+    uint32_t count[2];
+    uint32_t overflow[2];
+    float tau_final[2];  // the consumers' last bound of the row (<= its k-th largest value)
+    float warp_tau[2][kConsumerWarps];
+    float st_max[2][kConsumerWarps];
+    float st_sum[2][kConsumerWarps];
+    uint32_t st_cnt[2][kConsumerWarps];
+    uint32_t chist[256];
+    uint32_t csel[2];
     uint32_t error;
     uint32_t issued;
-    uint32_t n;
-    uint32_t red32[kThreads / 32];
-    unsigned long long red64[kThreads / 32];
-    float redf[kThreads / 32];
-    float bcast_f[2];
-    uint32_t bcast_u[2];
 };
 
 // Geometry of one row: a scalar head up to 16-byte alignment, a body of
@@ -79,304 +107,391 @@ __device__ __forceinline__ RowGeom row_geom(const float *logits, size_t row, siz
     return g;
 }
 
-// Warp-aggregated append of (key, idx) when `take`.
-__device__ __forceinline__ void append_candidate(StreamSmem &sm, bool take, uint32_t key,
-                                                 uint32_t idx) {
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Barrier of the consumer warps that also ORs a predicate across them: every
+// consumer thread gets the same answer.
+__device__ __forceinline__ bool consumers_any(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"(p ? 1u : 0u), "n"(kBarConsumers), "n"(kConsumers)
+        : "memory");
+    return r != 0;
+}
+
+// Appends the logits of a float4 group that pass `tau` (one shared atomic per
+// lane that has any). Returns true if the list grew past `mark`.
+__device__ __forceinline__ bool append_group(CandList &L, uint32_t *count, uint32_t *overflow,
+                                             float tau, float v0, float v1, float v2, float v3,
+                                             uint32_t i0, uint32_t mark) {
+    const uint32_t c = (v0 >= tau ? 1u : 0u) + (v1 >= tau ? 1u : 0u) + (v2 >= tau ? 1u : 0u) +
+                       (v3 >= tau ? 1u : 0u);
+    if (!c) return false;
+    uint32_t pos = atomicAdd(count, c);
+    const float v[4] = {v0, v1, v2, v3};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (v[q] >= tau) {
+            if (pos < kCap) {
+                L.key[pos] = total_key(v[q]);
+                L.idx[pos] = i0 + q;
+            } else {
+                *overflow = 1;
+            }
+            ++pos;
+        }
+    }
+    return pos > mark;
+}
+
+// Warp-aggregated append of (key, idx) when `take`. Returns true if this
+// warp's append reached position `mark` or beyond.
+__device__ __forceinline__ bool append_candidate(CandList &L, uint32_t *count, uint32_t *overflow,
+                                                 bool take, uint32_t key, uint32_t idx,
+                                                 uint32_t mark) {
     const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-    if (!ballot) return;
+    if (!ballot) return false;
     const int lane = threadIdx.x & 31;
     const int leader = __ffs(ballot) - 1;
     uint32_t base = 0;
-    if (lane == leader) base = atomicAdd(&sm.count, static_cast<uint32_t>(__popc(ballot)));
+    if (lane == leader) base = atomicAdd(count, static_cast<uint32_t>(__popc(ballot)));
     base = __shfl_sync(0xffffffffu, base, leader);
     if (take) {
         uint32_t pos = base + __popc(ballot & ((1u << lane) - 1u));
         if (pos < kCap) {
-            sm.u.cand.key[pos] = key;
-            sm.u.cand.idx[pos] = idx;
+            L.key[pos] = key;
+            L.idx[pos] = idx;
         } else {
-            sm.overflow = 1;
+            *overflow = 1;
         }
     }
+    return base + __popc(ballot) > mark;
 }
 
-__device__ __forceinline__ uint32_t relax_tau(uint32_t t) {
-    // A threshold of +0.0 also keeps -0.0: -0.0 < +0.0 is false in IEEE.
-    return t == kKeyPosZero ? kKeyNegZero : t;
-}
-
-// Raises tau to the k-th largest candidate key and drops candidates below it.
-__device__ void compact(StreamSmem &sm, uint32_t k, uint32_t &tau) {
-    __syncthreads();
-    const uint32_t count = min(sm.count, kCap);
-    if (count < k) return;  // uniform: every thread read the same count
-    uint32_t kth = block_select_kth_largest<kThreads>(
-        count, k, [&](uint32_t i) { return sm.u.cand.key[i]; }, sm.hist, sm.sel);
-    uint32_t nt = relax_tau(kth);
-    if (nt > tau) tau = nt;
-    constexpr int kPer = kCap / kThreads;
-    uint32_t kk[kPer], ii[kPer];
+// Each warp's t-th largest lane maximum, written for the consumers' next
+// barrier (double-buffered by `par`).
+__device__ __forceinline__ void post_warp_bound(StreamSmem &sm, float lmax, uint32_t t, int cw,
+                                                uint32_t par) {
+    const int lane = threadIdx.x & 31;
+    float m = lmax;
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-        uint32_t i = threadIdx.x + q * kThreads;
-        kk[q] = i < count ? sm.u.cand.key[i] : 0u;
-        ii[q] = i < count ? sm.u.cand.idx[i] : 0u;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) sm.count = 0;
-    __syncthreads();
+    for (int k = 2; k <= 32; k <<= 1) {
 #pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-        uint32_t i = threadIdx.x + q * kThreads;
-        append_candidate(sm, i < count && kk[q] >= tau, kk[q], ii[q]);
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float o = __shfl_xor_sync(0xffffffffu, m, j);
+            const bool ascending = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            m = (lower == ascending) ? fminf(m, o) : fmaxf(m, o);
+        }
     }
-    __syncthreads();
+    // Ascending across lanes: lane 32 - t holds the t-th largest.
+    const float bound = __shfl_sync(0xffffffffu, m, 32 - static_cast<int>(t));
+    if (lane == 0) sm.warp_tau[par][cw] = bound;
 }
 
-// Finishes a row from its candidate list: exact threshold, survivors, top-p,
-// softmax, argmax or draw. Writes the row's outputs.
-__device__ void finish_row(StreamSmem &sm, const CallParams &cp, size_t row, uint32_t *out_ids,
-                           int32_t *out_status, float *out_probs) {
-    __syncthreads();
-    const uint32_t count = min(sm.count, kCap);
+__device__ __forceinline__ float read_bound(const StreamSmem &sm, uint32_t par) {
+    float b = sm.warp_tau[par][0];
+#pragma unroll
+    for (int w = 1; w < kConsumerWarps; ++w) b = fminf(b, sm.warp_tau[par][w]);
+    return b;
+}
+
+// --- finisher (one warp) ------------------------------------------------------
+
+// s <- fl(s + v[i]) over i in order (one lane; loads batched ahead of the adds).
+__device__ __forceinline__ float chain_sum(const float *v, uint32_t n, float s) {
+    uint32_t i = 0;
+    for (; i + 8 <= n; i += 8) {
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = v[i + q];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) s = __fadd_rn(s, t[q]);
+    }
+    for (; i < n; ++i) s = __fadd_rn(s, v[i]);
+    return s;
+}
+
+// First i whose running sum (from +0) after v[i] exceeds p (candidates.rs:67-75); n if none.
+__device__ __forceinline__ uint32_t chain_cut_above(const float *v, uint32_t n, float p) {
+    float s = 0.0f;
+    uint32_t i = 0;
+    for (; i + 8 <= n; i += 8) {
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = v[i + q];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            s = __fadd_rn(s, t[q]);
+            if (s > p) return i + q;
+        }
+    }
+    for (; i < n; ++i) {
+        s = __fadd_rn(s, v[i]);
+        if (s > p) return i;
+    }
+    return n;
+}
+
+// sample_multinomial's loop (sampler.rs:111-121): first i with r < cumsum.
+__device__ __forceinline__ uint32_t chain_draw(const float *v, uint32_t n, float r, float *lo,
+                                               float *hi) {
+    float s = 0.0f;
+    uint32_t i = 0;
+    for (; i + 8 <= n; i += 8) {
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = v[i + q];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float b = s;
+            s = __fadd_rn(s, t[q]);
+            if (r < s) {
+                *lo = b;
+                *hi = s;
+                return i + q;
+            }
+        }
+    }
+    for (; i < n; ++i) {
+        const float b = s;
+        s = __fadd_rn(s, v[i]);
+        if (r < s) {
+            *lo = b;
+            *hi = s;
+            return i;
+        }
+    }
+    *lo = s;
+    *hi = s;
+    return n;
+}
+
+__device__ __forceinline__ uint32_t pow2_at_least(uint32_t n) {
+    uint32_t p = 32;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+// Survivors of the keep test against `thr` packed into fw.items (warp ballot
+// compaction); returns their number.
+template <typename Pack>
+__device__ __forceinline__ uint32_t gather_survivors(FinishWork &fw, const uint32_t *ckey,
+                                                     const uint32_t *cidx, uint32_t count,
+                                                     Pack pack) {
+    const int lane = threadIdx.x & 31;
+    uint32_t n = 0;
+    for (uint32_t base = 0; base < count; base += 32) {
+        const uint32_t i = base + lane;
+        bool keep = false;
+        unsigned long long it = 0;
+        if (i < count) keep = pack(ckey[i], cidx[i], &it);
+        const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+        if (keep) fw.items[n + __popc(ballot & ((1u << lane) - 1u))] = it;
+        n += __popc(ballot);
+    }
+    return n;
+}
+
+// Drops, in place, the candidates below `tau` (one warp). tau is at most the
+// row's k-th largest value, so nothing dropped could survive top-k; an IEEE
+// compare keeps -0.0 against +0.0 as the keep test does.
+__device__ __forceinline__ uint32_t precut_list(CandList &L, uint32_t count, float tau) {
+    const int lane = threadIdx.x & 31;
+    uint32_t n = 0;
+    for (uint32_t base = 0; base < count; base += 32) {
+        const uint32_t i = base + lane;
+        uint32_t key = 0, idx = 0;
+        bool keep = false;
+        if (i < count) {
+            key = L.key[i];
+            idx = L.idx[i];
+            keep = key_to_float(key) >= tau;
+        }
+        const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            const uint32_t pos = n + __popc(ballot & ((1u << lane) - 1u));
+            L.key[pos] = key;
+            L.idx[pos] = idx;
+        }
+        n += __popc(ballot);
+        __syncwarp();
+    }
+    return n;
+}
+
+// Finishes a row from its candidate list (one warp). Writes the row's outputs.
+__device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *ckey,
+                            const uint32_t *cidx, uint32_t count, const CallParams &cp, size_t row,
+                            uint32_t *out_ids, int32_t *out_status, float *out_probs) {
+    const int lane = threadIdx.x & 31;
     // Exact top-k threshold (candidates.rs:38-43). With fewer than k
     // candidates every candidate survives (the k-th largest is then -inf or
-    // below, which keeps all values that are not -inf).
+    // below, which keeps every value that is not -inf).
     float thr = kNegInf;
     if (cp.topk_active && count >= cp.top_k) {
-        uint32_t kth = block_select_kth_largest<kThreads>(
-            count, cp.top_k, [&](uint32_t i) { return sm.u.cand.key[i]; }, sm.hist, sm.sel);
+        const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
+            count, cp.top_k, [&](uint32_t i) { return ckey[i]; }, fw.hist, fw.sel);
         thr = key_to_float(kth);
     }
-    // Survivors, packed for a (value desc, index asc) sort when top-p is on,
-    // else (index asc).
-    constexpr int kPer = kCap / kThreads;
-    unsigned long long it[kPer];
-    bool keep[kPer];
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-        uint32_t i = threadIdx.x + q * kThreads;
-        keep[q] = false;
-        it[q] = 0;
-        if (i < count) {
-            uint32_t key = sm.u.cand.key[i];
-            uint32_t idx = sm.u.cand.idx[i];
-            keep[q] = survives(key_to_float(key), thr);
-            it[q] = cp.topp_active ? pack_key_index(~key, idx) : pack_key_index(idx, key);
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) sm.n = 0;
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-        const uint32_t ballot = __ballot_sync(0xffffffffu, keep[q]);
-        if (!ballot) continue;
-        const int lane = threadIdx.x & 31;
-        const int leader = __ffs(ballot) - 1;
-        uint32_t base = 0;
-        if (lane == leader) base = atomicAdd(&sm.n, static_cast<uint32_t>(__popc(ballot)));
-        base = __shfl_sync(0xffffffffu, base, leader);
-        if (keep[q]) sm.u.items[base + __popc(ballot & ((1u << lane) - 1u))] = it[q];
-    }
-    __syncthreads();
-    uint32_t n = sm.n;
-    uint32_t n64 = 32;
-    while (n64 < n) n64 <<= 1;
-    for (uint32_t i = n + threadIdx.x; i < n64; i += kThreads) sm.u.items[i] = ~0ull;
-    block_bitonic_sort<kThreads>(sm.u.items, n64);
+    const bool topp = cp.topp_active;
+    uint32_t n = gather_survivors(fw, ckey, cidx, count,
+                                  [&](uint32_t key, uint32_t idx, unsigned long long *it) {
+                                      *it = topp ? pack_key_index(~key, idx) : pack_key_index(idx, key);
+                                      return survives(key_to_float(key), thr);
+                                  });
+    uint32_t n64 = pow2_at_least(n);
+    for (uint32_t i = n + lane; i < n64; i += 32) fw.items[i] = ~0ull;
+    group_bitonic_sort<32, SyncWarp>(fw.items, n64);
 
-    if (cp.topp_active && n > 0) {
-        // Candidates::top_p, candidates.rs:55-78: items are (~key, idx)
+    if (topp && n > 0) {
+        // Candidates::top_p (candidates.rs:55-78): items are (~key, idx)
         // ascending = value descending, index ascending.
-        const float maxv = key_to_float(~static_cast<uint32_t>(sm.u.items[0] >> 32));
-        for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
-            float v = key_to_float(~static_cast<uint32_t>(sm.u.items[i] >> 32));
-            sm.vals[i] = expf_ref(__fsub_rn(v, maxv), sm.exp_tab);
+        const float maxv = key_to_float(~static_cast<uint32_t>(fw.items[0] >> 32));
+        for (uint32_t i = lane; i < n; i += 32)
+            fw.vals[i] = expf_ref(__fsub_rn(key_to_float(~static_cast<uint32_t>(fw.items[i] >> 32)), maxv), tab);
+        __syncwarp();
+        float exp_sum = 0.0f;
+        if (lane == 0) exp_sum = chain_sum(fw.vals, n, 0.0f);  // fold(0.0, +)
+        exp_sum = __shfl_sync(0xffffffffu, exp_sum, 0);
+        for (uint32_t i = lane; i < n; i += 32) fw.vals[i] = __fdiv_rn(fw.vals[i], exp_sum);
+        __syncwarp();
+        uint32_t cut = 0;
+        if (lane == 0) {
+            const uint32_t at = chain_cut_above(fw.vals, n, cp.top_p);
+            cut = at < n ? at + 1 : n;
         }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float exp_sum = 0.0f;
-            for (uint32_t i = 0; i < n; ++i) exp_sum = __fadd_rn(exp_sum, sm.vals[i]);
-            float cumsum = 0.0f;
-            uint32_t cutoff = n;
-            for (uint32_t i = 0; i < n; ++i) {
-                cumsum = __fadd_rn(cumsum, __fdiv_rn(sm.vals[i], exp_sum));
-                if (cumsum > cp.top_p) {
-                    cutoff = i + 1;
-                    break;
-                }
-            }
-            sm.n = cutoff;
-        }
-        __syncthreads();
-        n = sm.n;
+        n = __shfl_sync(0xffffffffu, cut, 0);
         // Re-key the kept prefix by index and sort it back to index order.
-        for (uint32_t i = threadIdx.x; i < n64; i += kThreads) {
-            unsigned long long x = sm.u.items[i];
-            uint32_t key = ~static_cast<uint32_t>(x >> 32);
-            uint32_t idx = static_cast<uint32_t>(x);
-            sm.u.items[i] = i < n ? pack_key_index(idx, key) : ~0ull;
+        for (uint32_t i = lane; i < n64; i += 32) {
+            const unsigned long long x = fw.items[i];
+            fw.items[i] = i < n ? pack_key_index(static_cast<uint32_t>(x), ~static_cast<uint32_t>(x >> 32))
+                                : ~0ull;
         }
-        block_bitonic_sort<kThreads>(sm.u.items, n64);
+        group_bitonic_sort<32, SyncWarp>(fw.items, n64);
     }
 
-    if (cp.out_nsurv && threadIdx.x == 0) cp.out_nsurv[row] = n;
+    if (cp.out_nsurv && lane == 0) cp.out_nsurv[row] = n;
     if (cp.out_surv) {
         const uint32_t m = min(n, cp.surv_cap);
-        for (uint32_t i = threadIdx.x; i < m; i += kThreads)
-            cp.out_surv[row * cp.surv_cap + i] = static_cast<uint32_t>(sm.u.items[i] >> 32);
+        for (uint32_t i = lane; i < m; i += 32)
+            cp.out_surv[row * cp.surv_cap + i] = static_cast<uint32_t>(fw.items[i] >> 32);
     }
 
     // softmax (filters.rs:5-15) over the survivors in index order.
     float mx = kNegInf;
     unsigned long long amax = 0;
-    for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
-        uint32_t key = static_cast<uint32_t>(sm.u.items[i]);
+    for (uint32_t i = lane; i < n; i += 32) {
+        const uint32_t key = static_cast<uint32_t>(fw.items[i]);
         mx = fmaxf(mx, key_to_float(key));
-        unsigned long long c = pack_key_index(key, i);
+        const unsigned long long c = pack_key_index(key, i);
         amax = c > amax ? c : amax;
     }
-    mx = block_reduce<kThreads>(mx, sm.redf, OpFMax());
-    amax = block_reduce<kThreads>(amax, sm.red64, OpMaxU64());
-    for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
-        float v = key_to_float(static_cast<uint32_t>(sm.u.items[i]));
-        sm.vals[i] = expf_ref(__fsub_rn(v, mx), sm.exp_tab);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const unsigned long long a = __shfl_xor_sync(0xffffffffu, amax, o);
+        amax = a > amax ? a : amax;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = -0.0f;  // <f32 as Sum>::sum
-        for (uint32_t i = 0; i < n; ++i) s = __fadd_rn(s, sm.vals[i]);
-        sm.bcast_f[0] = s;
-    }
-    __syncthreads();
-    const float sum = sm.bcast_f[0];
+    for (uint32_t i = lane; i < n; i += 32)
+        fw.vals[i] = expf_ref(__fsub_rn(key_to_float(static_cast<uint32_t>(fw.items[i])), mx), tab);
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0) sum = chain_sum(fw.vals, n, -0.0f);  // <f32 as Sum>::sum folds from -0.0
+    sum = __shfl_sync(0xffffffffu, sum, 0);
     const bool norm = (fabsf(sum) < kPosInf) && sum > 0.0f;
-    uint32_t valid = 0;
-    for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
-        float pi = sm.vals[i];
+    bool valid = false;
+    for (uint32_t i = lane; i < n; i += 32) {
+        float pi = fw.vals[i];
         if (norm) pi = __fdiv_rn(pi, sum);
-        sm.vals[i] = pi;
-        if (!(pi != pi || pi <= 0.0f)) valid = 1;
+        fw.vals[i] = pi;
+        if (!(pi != pi || pi <= 0.0f)) valid = true;
     }
-    valid = block_reduce<kThreads>(valid, sm.red32, OpOrU32());
-    if (threadIdx.x == 0) {
+    valid = __any_sync(0xffffffffu, valid);
+    __syncwarp();
+    if (lane == 0) {
         int32_t status = RSC_ROW_NO_VALID_TOKENS;
         uint32_t token = 0;
         float prob = __uint_as_float(0x7fc00000u);
         if (valid) {
             uint32_t pos;
+            status = RSC_ROW_OK;
             if (cp.argmax_branch) {
                 pos = static_cast<uint32_t>(amax);
             } else {
                 const float r = row_uniform(cp, row);
-                float cumsum = 0.0f, before = 0.0f;
-                pos = n - 1;
-                bool hit = false;
-                for (uint32_t i = 0; i < n; ++i) {
-                    before = cumsum;
-                    cumsum = __fadd_rn(cumsum, sm.vals[i]);
-                    if (r < cumsum) {
-                        pos = i;
-                        hit = true;
-                        break;
-                    }
-                }
-                if (!hit) before = cumsum;
-                status = 0;
-                if (fabsf(r - cumsum) < 1e-6f || fabsf(r - before) < 1e-6f)
+                float lo, hi;
+                pos = chain_draw(fw.vals, n, r, &lo, &hi);
+                if (pos >= n) pos = n - 1;
+                if (fabsf(r - hi) < 1e-6f || fabsf(r - lo) < 1e-6f)
                     status |= RSC_ROW_FLAG_DRAW_NEAR_BOUNDARY;
             }
-            token = static_cast<uint32_t>(sm.u.items[pos] >> 32);
-            prob = sm.vals[pos];
-            status = (status & ~0xff) | RSC_ROW_OK;
+            token = static_cast<uint32_t>(fw.items[pos] >> 32);
+            prob = fw.vals[pos];
         }
         out_ids[row] = token;
         out_status[row] = status;
         if (out_probs) out_probs[row] = prob;
     }
-    __syncthreads();
+    __syncwarp();
 }
 
-// Shard record of the vocab-sharded mode: the scaled row maximum and online
-// exp-sum of the shard, and every logit of the shard at or above its local
-// k-th largest key (which is at most the global one), sorted (key desc,
-// index asc) and capped at k + RSC_SHARD_TIE_CAP entries.
-__device__ void record_row(StreamSmem &sm, const CallParams &cp, size_t row, float mx_t,
-                           float se_t, uint32_t cnt_t, unsigned char *records, size_t rec_bytes) {
-    __syncthreads();
-    const uint32_t count = min(sm.count, kCap);
+// Shard record of the vocab-sharded mode (one warp): every candidate at or
+// above the shard's k-th largest key, sorted (key desc, index asc), capped at
+// k + RSC_SHARD_TIE_CAP entries, plus the shard's row statistics.
+__device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t *cidx,
+                            uint32_t count, const CallParams &cp, float M, float S, uint32_t nfin,
+                            unsigned char *rec) {
+    const int lane = threadIdx.x & 31;
     const uint32_t cap_entries = cp.top_k + RSC_SHARD_TIE_CAP;
     uint32_t floor_key = kKeyNegInf + 1u;
     if (count >= cp.top_k) {
-        uint32_t kth = block_select_kth_largest<kThreads>(
-            count, cp.top_k, [&](uint32_t i) { return sm.u.cand.key[i]; }, sm.hist, sm.sel);
-        floor_key = relax_tau(kth);
+        const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
+            count, cp.top_k, [&](uint32_t i) { return ckey[i]; }, fw.hist, fw.sel);
+        // A +0.0 threshold also keeps -0.0 (IEEE -0.0 < +0.0 is false).
+        floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
     }
-    constexpr int kPer = kCap / kThreads;
-    unsigned long long it[kPer];
-    bool keep[kPer];
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-        uint32_t i = threadIdx.x + q * kThreads;
-        keep[q] = false;
-        it[q] = 0;
-        if (i < count) {
-            uint32_t key = sm.u.cand.key[i];
-            keep[q] = key >= floor_key;
-            it[q] = pack_key_index(~key, sm.u.cand.idx[i]);
-        }
-    }
-    // Row statistics: max, sum of exp(v - max) rescaled per thread, count.
-    const float M = block_reduce<kThreads>(mx_t, sm.redf, OpFMax());
-    float se_scaled = (se_t > 0.0f) ? se_t * __expf(mx_t - M) : 0.0f;
-    se_scaled = block_reduce<kThreads>(se_scaled, sm.redf, [](float a, float b) { return a + b; });
-    const uint32_t nfin = block_reduce<kThreads>(cnt_t, sm.red32, OpAddU32());
-    __syncthreads();
-    if (threadIdx.x == 0) sm.n = 0;
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-        const uint32_t ballot = __ballot_sync(0xffffffffu, keep[q]);
-        if (!ballot) continue;
-        const int lane = threadIdx.x & 31;
-        const int leader = __ffs(ballot) - 1;
-        uint32_t base = 0;
-        if (lane == leader) base = atomicAdd(&sm.n, static_cast<uint32_t>(__popc(ballot)));
-        base = __shfl_sync(0xffffffffu, base, leader);
-        if (keep[q]) sm.u.items[base + __popc(ballot & ((1u << lane) - 1u))] = it[q];
-    }
-    __syncthreads();
-    const uint32_t n = sm.n;
-    uint32_t n64 = 32;
-    while (n64 < n) n64 <<= 1;
-    for (uint32_t i = n + threadIdx.x; i < n64; i += kThreads) sm.u.items[i] = ~0ull;
-    block_bitonic_sort<kThreads>(sm.u.items, n64);
+    const uint32_t n = gather_survivors(fw, ckey, cidx, count,
+                                        [&](uint32_t key, uint32_t idx, unsigned long long *it) {
+                                            *it = pack_key_index(~key, idx);
+                                            return key >= floor_key;
+                                        });
+    const uint32_t n64 = pow2_at_least(n);
+    for (uint32_t i = n + lane; i < n64; i += 32) fw.items[i] = ~0ull;
+    group_bitonic_sort<32, SyncWarp>(fw.items, n64);
     const uint32_t nc = min(n, cap_entries);
-    unsigned char *rec = records + row * rec_bytes;
     ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
     uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
     uint32_t *ridx = rkey + cap_entries;
-    for (uint32_t i = threadIdx.x; i < nc; i += kThreads) {
-        unsigned long long x = sm.u.items[i];
+    for (uint32_t i = lane; i < nc; i += 32) {
+        const unsigned long long x = fw.items[i];
         rkey[i] = ~static_cast<uint32_t>(x >> 32);
         ridx[i] = static_cast<uint32_t>(x);
     }
-    if (threadIdx.x == 0) {
+    if (lane == 0) {
         h->max_scaled = M;
-        h->sum_exp = se_scaled;
+        h->sum_exp = S;
         h->n_finite = nfin;
         h->n_cand = nc;
         h->n_dropped = n - nc;
-        h->last_key = nc ? ~static_cast<uint32_t>(sm.u.items[nc - 1] >> 32) : 0u;
+        h->last_key = nc ? ~static_cast<uint32_t>(fw.items[nc - 1] >> 32) : 0u;
         h->flags = 0;
         h->reserved = 0;
     }
-    __syncthreads();
+    __syncwarp();
 }
 
+// --- the streaming kernel -------------------------------------------------------
+
 template <bool kRecord>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 1)
 stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab,
                    size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs,
@@ -384,51 +499,141 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                    uint32_t index_offset, unsigned char *__restrict__ records, size_t rec_bytes) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     StreamSmem &sm = *reinterpret_cast<StreamSmem *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     load_exp_table(sm.exp_tab);
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], kConsumerWarps);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sm.list_full[b], 1);
+            mbar_init(&sm.list_empty[b], 1);
+        }
         sm.error = 0;
         sm.issued = 0;
         fence_barrier_init();
     }
-    __syncthreads();
+    __syncthreads();  // the last block-wide barrier: the roles split here
 
-    // Producer cursor over this CTA's (row, chunk) sequence; thread 0 only.
-    size_t prow = blockIdx.x;
-    uint32_t pchunk = 0;
-    uint32_t issued = 0;
-    auto produce_one = [&]() {
-        while (prow < rows) {
-            RowGeom g = row_geom(logits, prow, row_stride, vocab);
-            if (pchunk < g.nchunks) {
-                uint32_t off = g.head + pchunk * kChunk;
-                uint32_t len = min(kChunk, g.nbody - pchunk * kChunk);
-                uint32_t s = issued % kStages;
+    if (warp == kProducerWarp) {
+        if (lane != 0) return;
+        uint32_t q = 0;
+        bool ok = true;
+        for (size_t row = blockIdx.x; row < rows && ok; row += gridDim.x) {
+            const RowGeom g = row_geom(logits, row, row_stride, vocab);
+            for (uint32_t c = 0; c < g.nchunks; ++c) {
+                const uint32_t s = q % kStages;
+                if (q >= kStages && !mbar_wait(&sm.empty[s], ((q / kStages) - 1u) & 1u)) {
+                    atomicExch(&sm.error, 1u);
+                    ok = false;
+                    break;
+                }
+                if (*static_cast<volatile uint32_t *>(&sm.error)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t len = min(kChunk, g.nbody - c * kChunk);
                 mbar_arrive_expect_tx(&sm.full[s], len * 4u);
-                tma_load_1d(sm.ring[s], g.p + off, len * 4u, &sm.full[s]);
-                ++issued;
-                ++pchunk;
-                sm.issued = issued;
-                return;
+                tma_load_1d(sm.ring[s], g.p + g.head + c * kChunk, len * 4u, &sm.full[s]);
+                ++q;
             }
-            prow += gridDim.x;
-            pchunk = 0;
         }
-    };
-    if (threadIdx.x == 0)
-        for (uint32_t s = 0; s < kStages; ++s) produce_one();
+        // Before this thread exits, every copy it issued has landed (bounded):
+        // the last phase of each stage.
+        const uint32_t first = q > kStages ? q - kStages : 0u;
+        for (uint32_t i = first; i < q; ++i) mbar_wait(&sm.full[i % kStages], (i / kStages) & 1u);
+        return;
+    }
 
-    uint32_t consumed = 0;
-    size_t row = blockIdx.x;
-    for (; row < rows; row += gridDim.x) {
+    if (warp == kFinisherWarp) {
+        uint32_t j = 0;
+        size_t row = blockIdx.x;
+        for (; row < rows; row += gridDim.x, ++j) {
+            const uint32_t b = j & 1u;
+            const bool got = mbar_wait(&sm.list_full[b], (j >> 1) & 1u);
+            if (__any_sync(0xffffffffu, !got)) {
+                if (lane == 0) atomicExch(&sm.error, 1u);
+                break;
+            }
+            uint32_t cnt = sm.count[b];
+            const bool ov = sm.overflow[b] != 0 || cnt > kCap;
+            if (!ov && cp.topk_active) cnt = precut_list(sm.list[b], cnt, sm.tau_final[b]);
+            if (kRecord) {
+                unsigned char *rec = records + row * rec_bytes;
+                if (ov) {
+                    if (lane == 0) {
+                        ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                        h->flags = 1;
+                        h->n_cand = 0;
+                        h->n_dropped = 0;
+                    }
+                } else {
+                    float M = kNegInf;
+                    uint32_t nfin = 0;
+                    for (int w = 0; w < kConsumerWarps; ++w) {
+                        M = fmaxf(M, sm.st_max[b][w]);
+                        nfin += sm.st_cnt[b][w];
+                    }
+                    float S = 0.0f;
+                    for (int w = 0; w < kConsumerWarps; ++w)
+                        if (sm.st_sum[b][w] > 0.0f) S += sm.st_sum[b][w] * __expf(sm.st_max[b][w] - M);
+                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, M, S, nfin, rec);
+                }
+            } else {
+                if (ov) {
+                    if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
+                } else {
+                    finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, cnt, cp, row,
+                                out_ids, out_status, out_probs);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.list_empty[b]);
+        }
+        if (lane == 0) {
+            // Rows this warp could not finish because a wait gave up.
+            for (; row < rows; row += gridDim.x) {
+                if (kRecord) {
+                    reinterpret_cast<ShardRecordHeader *>(records + row * rec_bytes)->flags = 2;
+                } else {
+                    out_ids[row] = 0;
+                    out_status[row] = RSC_ROW_INTERNAL;
+                }
+            }
+        }
+        return;
+    }
+
+    // Consumers: warps 0 .. kConsumerWarps-1.
+    const int cw = warp;
+    const float scale = cp.scale;
+    const uint32_t t_bound = cp.topk_active ? (cp.top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
+    uint32_t consumed = 0, par = 0, j = 0;
+    for (size_t row = blockIdx.x; row < rows; row += gridDim.x, ++j) {
+        const uint32_t b = j & 1u;
+        bool bad = false;
+        if (threadIdx.x == 0) {
+            if (j >= 2 && !mbar_wait(&sm.list_empty[b], ((j >> 1) - 1u) & 1u)) bad = true;
+            sm.count[b] = 0;
+            sm.overflow[b] = 0;
+        }
+        if (consumers_any(bad || *static_cast<volatile uint32_t *>(&sm.error) != 0)) break;
+        CandList &L = sm.list[b];
+        uint32_t *count = &sm.count[b];
+        uint32_t *ovf = &sm.overflow[b];
         const RowGeom g = row_geom(logits, row, row_stride, vocab);
-        uint32_t tau = kKeyNegInf + 1u;  // excludes -inf; everything else is a candidate
+        // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
+        // NaN (NaN reads as -inf in the reference, and -inf never survives);
+        // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
+        float tau = -3.402823466e38f;
+        float lmax = kNegInf;
         float mx_t = kNegInf, se_t = 0.0f;
         uint32_t cnt_t = 0;
         auto stats = [&](float v) {
             if (kRecord) {
-                if (v != kNegInf) {
+                if (v != kNegInf && v == v) {
                     ++cnt_t;
                     if (v > mx_t) {
                         se_t = (mx_t == kNegInf ? 0.0f : se_t * __expf(mx_t - v)) + 1.0f;
@@ -439,188 +644,219 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 }
             }
         };
-        if (threadIdx.x == 0) {
-            sm.count = 0;
-            sm.overflow = 0;
-        }
-        __syncthreads();
-        // Scalar head and tail.
+        // Scalar head and tail (at most 3 logits each).
         {
-            uint32_t ntail = vocab - g.head - g.nbody;
-            uint32_t i = threadIdx.x;
-            bool take = false;
-            uint32_t key = 0, idx = ~0u;
+            const uint32_t ntail = vocab - g.head - g.nbody;
+            const uint32_t i = threadIdx.x;
+            uint32_t idx = ~0u;
             if (i < g.head) idx = i;
             else if (i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
+            float v = kNegInf;
             if (idx != ~0u) {
-                float v = scale_logit(g.p[idx], cp.scale);
+                v = __fmul_rn(g.p[idx], scale);
                 stats(v);
-                key = total_key(v);
-                take = key >= tau;
+                lmax = fmaxf(lmax, v);
             }
-            append_candidate(sm, take, key, idx + index_offset);
+            append_candidate(L, count, ovf, v >= tau, total_key(v), idx + index_offset, kCap);
         }
+        bool stop = false;
+        bool got = true, mark = false;
         for (uint32_t c = 0; c < g.nchunks; ++c) {
             const uint32_t s = consumed % kStages;
-            const uint32_t parity = (consumed / kStages) & 1u;
-            if (!mbar_wait(&sm.full[s], parity)) atomicExch(&sm.error, 1u);
+            got &= mbar_wait(&sm.full[s], (consumed / kStages) & 1u);
             const uint32_t len = min(kChunk, g.nbody - c * kChunk);
-            const uint32_t base_idx = g.head + c * kChunk + index_offset;
             const float4 *r4 = reinterpret_cast<const float4 *>(sm.ring[s]);
+            const uint32_t base_idx = g.head + c * kChunk + index_offset;
+            if (c == 0 && t_bound) {
+                // First chunk: lane maxima before filtering, so that tau is
+                // already high for this chunk's own logits.
 #pragma unroll
-            for (uint32_t jj = 0; jj < kChunk / 4 / kThreads; ++jj) {
-                const uint32_t j = threadIdx.x + jj * kThreads;
-                float4 f = (4 * j < len) ? r4[j] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
-                const uint32_t i0 = base_idx + 4 * j;
-                const float v0 = scale_logit(f.x, cp.scale), v1 = scale_logit(f.y, cp.scale);
-                const float v2 = scale_logit(f.z, cp.scale), v3 = scale_logit(f.w, cp.scale);
+                for (uint32_t jj = 0; jj < kChunk / 4 / kConsumers; ++jj) {
+                    const uint32_t q = threadIdx.x + jj * kConsumers;
+                    if (4 * q < len) {
+                        const float4 f = r4[q];
+                        lmax = fmaxf(fmaxf(lmax, fmaxf(__fmul_rn(f.x, scale), __fmul_rn(f.y, scale))),
+                                     fmaxf(__fmul_rn(f.z, scale), __fmul_rn(f.w, scale)));
+                    }
+                }
+                post_warp_bound(sm, lmax, t_bound, cw, par);
+                if (consumers_any(!got)) {
+                    stop = true;
+                    break;
+                }
+                tau = fmaxf(tau, read_bound(sm, par));
+                par ^= 1u;
+            }
+            constexpr uint32_t kPerThread = kChunk / 4 / kConsumers;
+            float4 f[kPerThread];
+#pragma unroll
+            for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                const uint32_t q = threadIdx.x + jj * kConsumers;
+                f[jj] = (4 * q < len) ? r4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage s released by this warp
+            ++consumed;
+#pragma unroll
+            for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                const uint32_t q = threadIdx.x + jj * kConsumers;
+                const float v0 = __fmul_rn(f[jj].x, scale), v1 = __fmul_rn(f[jj].y, scale);
+                const float v2 = __fmul_rn(f[jj].z, scale), v3 = __fmul_rn(f[jj].w, scale);
                 stats(v0);
                 stats(v1);
                 stats(v2);
                 stats(v3);
-                const uint32_t k0 = total_key(v0), k1 = total_key(v1);
-                const uint32_t k2 = total_key(v2), k3 = total_key(v3);
-                const bool any = (k0 >= tau) | (k1 >= tau) | (k2 >= tau) | (k3 >= tau);
-                if (__any_sync(0xffffffffu, any)) {
-                    append_candidate(sm, k0 >= tau, k0, i0);
-                    append_candidate(sm, k1 >= tau, k1, i0 + 1);
-                    append_candidate(sm, k2 >= tau, k2, i0 + 2);
-                    append_candidate(sm, k3 >= tau, k3, i0 + 3);
+                lmax = fmaxf(fmaxf(lmax, fmaxf(v0, v1)), fmaxf(v2, v3));
+                mark |= append_group(L, count, ovf, tau, v0, v1, v2, v3, base_idx + 4 * q, kCompactAt);
+            }
+            const bool last = c + 1 == g.nchunks;
+            if (!last && (c + 1) % kRefresh != 0) continue;
+            if (t_bound) post_warp_bound(sm, lmax, t_bound, cw, par);
+            // One barrier every kRefresh chunks: settles the list, publishes
+            // the bounds, and raises the rare events (a failed wait, a long
+            // list).
+            const bool want_compact = mark && cp.topk_active && !last;
+            mark = false;
+            if (consumers_any(!got || want_compact)) {
+                if (consumers_any(!got)) {
+                    stop = true;
+                    break;
+                }
+                // Compaction: tau rises to the list's own k-th largest value.
+                const uint32_t cnt = min(*count, kCap);
+                if (cnt >= cp.top_k) {
+                    const uint32_t kth = group_select_kth_largest<kConsumers, ConsumerSync>(
+                        cnt, cp.top_k, [&](uint32_t i) { return L.key[i]; }, sm.chist, sm.csel);
+                    tau = fmaxf(tau, key_to_float(kth));
+                    constexpr int kPer = kCap / kConsumers;
+                    uint32_t kk[kPer], ii[kPer];
+#pragma unroll
+                    for (int e = 0; e < kPer; ++e) {
+                        const uint32_t i = threadIdx.x + e * kConsumers;
+                        kk[e] = i < cnt ? L.key[i] : 0u;
+                        ii[e] = i < cnt ? L.idx[i] : 0u;
+                    }
+                    ConsumerSync::sync();
+                    if (threadIdx.x == 0) *count = 0;
+                    ConsumerSync::sync();
+#pragma unroll
+                    for (int e = 0; e < kPer; ++e) {
+                        const uint32_t i = threadIdx.x + e * kConsumers;
+                        append_candidate(L, count, ovf, i < cnt && key_to_float(kk[e]) >= tau, kk[e],
+                                         ii[e], kCap);
+                    }
+                    ConsumerSync::sync();
+                    if (*count > kCompactAt && threadIdx.x == 0) *ovf = 1;
                 }
             }
-            __syncthreads();  // stage s fully read; candidate count settled
-            ++consumed;
-            if (threadIdx.x == 0) produce_one();
-            if (sm.error) break;
-            if (cp.topk_active && c + 1 < g.nchunks && sm.count > kCap - kChunk) {
-                compact(sm, cp.top_k, tau);
-                if (sm.count > kCap - kChunk) sm.overflow = 1;  // all threads write the same value
+            if (t_bound) {
+                tau = fmaxf(tau, read_bound(sm, par));
+                par ^= 1u;
             }
         }
-        __syncthreads();
-        if (sm.error) break;
+        if (stop) break;
         if (kRecord) {
-            if (sm.overflow || sm.count > kCap) {
-                if (threadIdx.x == 0) {
-                    ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(records + row * rec_bytes);
-                    h->flags = 1;
-                    h->n_cand = 0;
-                    h->n_dropped = 0;
-                }
-                __syncthreads();
-                continue;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float om = __shfl_xor_sync(0xffffffffu, mx_t, o);
+                const float os = __shfl_xor_sync(0xffffffffu, se_t, o);
+                const float m2 = fmaxf(mx_t, om);
+                se_t = (se_t > 0.0f ? se_t * __expf(mx_t - m2) : 0.0f) +
+                       (os > 0.0f ? os * __expf(om - m2) : 0.0f);
+                mx_t = m2;
+                cnt_t += __shfl_xor_sync(0xffffffffu, cnt_t, o);
             }
-            record_row(sm, cp, row, mx_t, se_t, cnt_t, records, rec_bytes);
-        } else {
-            if (sm.overflow || sm.count > kCap) {
-                if (threadIdx.x == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
-                __syncthreads();
-                continue;
+            if (lane == 0) {
+                sm.st_max[b][cw] = mx_t;
+                sm.st_sum[b][cw] = se_t;
+                sm.st_cnt[b][cw] = cnt_t;
             }
-            finish_row(sm, cp, row, out_ids, out_status, out_probs);
         }
+        if (threadIdx.x == 0) sm.tau_final[b] = tau;
+        ConsumerSync::sync();  // the row's list is complete
+        if (threadIdx.x == 0) mbar_arrive(&sm.list_full[b]);
     }
-    if (row < rows) {
-        // A wait gave up. Wait (bounded) for the copies still in flight into
-        // this CTA's shared memory, then report the unfinished rows.
-        if (threadIdx.x == 0) {
-            const uint32_t n_issued = sm.issued;
-            for (uint32_t q = consumed; q < n_issued; ++q)
-                mbar_wait(&sm.full[q % kStages], (q / kStages) & 1u);
-        }
-        for (; row < rows; row += gridDim.x) {
-            if (threadIdx.x != 0) continue;
-            if (kRecord) {
-                reinterpret_cast<ShardRecordHeader *>(records + row * rec_bytes)->flags = 2;
-            } else {
-                out_ids[row] = 0;
-                out_status[row] = RSC_ROW_INTERNAL;
-            }
-        }
-    }
+    // A consumer that left early does not wait for the others: the finisher's
+    // and producer's bounded waits end the CTA.
 }
 
-// Vocab-sharded merge: one CTA per row gathers the shards' records into the
-// candidate list and finishes the row exactly as the unsharded kernel does.
-__global__ void __launch_bounds__(kThreads)
+// Vocab-sharded merge: each warp gathers the shards' records of one row into
+// its candidate list and finishes the row exactly as the streaming kernel does.
+constexpr int kMergeWarps = 4;
+
+struct MergeSmem {
+    CandList list[kMergeWarps];
+    FinishWork fw[kMergeWarps];
+    double exp_tab[32];
+};
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
 shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, size_t rows,
                    size_t rec_bytes, CallParams cp, uint32_t *__restrict__ out_ids,
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    StreamSmem &sm = *reinterpret_cast<StreamSmem *>(smem_raw);
+    MergeSmem &sm = *reinterpret_cast<MergeSmem *>(smem_raw);
     load_exp_table(sm.exp_tab);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    CandList &L = sm.list[warp];
+    FinishWork &fw = sm.fw[warp];
     const uint32_t cap_entries = cp.top_k + RSC_SHARD_TIE_CAP;
-    for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
-        if (threadIdx.x == 0) {
-            sm.count = 0;
-            sm.overflow = 0;
-        }
-        __syncthreads();
+    for (size_t row = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; row < rows;
+         row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
+        uint32_t count = 0;
+        bool bad = false;
         for (size_t s = 0; s < n_shards; ++s) {
             const unsigned char *rec = records + (s * rows + row) * rec_bytes;
             const ShardRecordHeader *h = reinterpret_cast<const ShardRecordHeader *>(rec);
             const uint32_t *rkey = reinterpret_cast<const uint32_t *>(rec + sizeof(ShardRecordHeader));
             const uint32_t *ridx = rkey + cap_entries;
-            const uint32_t base = sm.count;
             const uint32_t nc = h->flags ? 0u : min(h->n_cand, cap_entries);
-            for (uint32_t i = threadIdx.x; i < nc; i += kThreads) {
-                if (base + i < kCap) {
-                    sm.u.cand.key[base + i] = rkey[i];
-                    sm.u.cand.idx[base + i] = ridx[i];
+            if (h->flags || count + nc > kCap) bad = true;
+            for (uint32_t i = lane; i < nc; i += 32) {
+                if (count + i < kCap) {
+                    L.key[count + i] = rkey[i];
+                    L.idx[count + i] = ridx[i];
                 }
             }
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                sm.count = base + nc;
-                if (h->flags || base + nc > kCap) sm.overflow = 1;
-            }
-            __syncthreads();
+            count += nc;
         }
-        bool bad = sm.overflow != 0;
-        if (!bad && cp.topk_active && sm.count >= cp.top_k) {
+        __syncwarp();
+        if (!bad) {
             // A shard that dropped tied entries is harmless only if everything
             // it dropped lies below the global threshold.
-            uint32_t kth = block_select_kth_largest<kThreads>(
-                sm.count, cp.top_k, [&](uint32_t i) { return sm.u.cand.key[i]; }, sm.hist, sm.sel);
-            const uint32_t floor_key = relax_tau(kth);
-            for (size_t s = 0; s < n_shards; ++s) {
-                const ShardRecordHeader *h =
-                    reinterpret_cast<const ShardRecordHeader *>(records + (s * rows + row) * rec_bytes);
-                if (h->n_dropped > 0 && h->last_key >= floor_key) bad = true;
+            uint32_t floor_key = 0u;
+            const bool have_kth = cp.topk_active && count >= cp.top_k;
+            if (have_kth) {
+                const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
+                    count, cp.top_k, [&](uint32_t i) { return L.key[i]; }, fw.hist, fw.sel);
+                floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
             }
-        } else if (!bad) {
             for (size_t s = 0; s < n_shards; ++s) {
                 const ShardRecordHeader *h =
                     reinterpret_cast<const ShardRecordHeader *>(records + (s * rows + row) * rec_bytes);
-                if (h->n_dropped > 0) bad = true;
+                if (h->n_dropped > 0 && (!have_kth || h->last_key >= floor_key)) bad = true;
             }
         }
         if (bad) {
-            if (threadIdx.x == 0) {
+            if (lane == 0) {
                 out_ids[row] = 0;
                 out_status[row] = RSC_ROW_INTERNAL;
                 if (out_probs) out_probs[row] = __uint_as_float(0x7fc00000u);
             }
-            __syncthreads();
+            __syncwarp();
             continue;
         }
-        finish_row(sm, cp, row, out_ids, out_status, out_probs);
+        finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
     }
 }
 
 template <typename K>
-cudaError_t grid_for(K kernel, size_t rows, int num_sms, size_t *grid) {
-    const size_t smem = sizeof(StreamSmem);
+cudaError_t prepare(K kernel, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) per_sm = 1;
-    size_t g = static_cast<size_t>(num_sms) * per_sm;
-    *grid = g > rows ? rows : g;
-    return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
 }
 
 }  // namespace
@@ -632,9 +868,9 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                int32_t *out_status, float *out_probs, uint32_t *large_rows,
                                uint32_t *large_count, int num_sms, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
-    size_t grid = 0;
-    cudaError_t e = grid_for(stream_topk_kernel<false>, rows, num_sms, &grid);
+    cudaError_t e = prepare(stream_topk_kernel<false>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
+    const size_t grid = rows < static_cast<size_t>(num_sms) ? rows : static_cast<size_t>(num_sms);
     stream_topk_kernel<false><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
         large_count, 0u, nullptr, 0);
@@ -646,9 +882,9 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
                                  void *records, size_t rec_bytes, int num_sms,
                                  cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
-    size_t grid = 0;
-    cudaError_t e = grid_for(stream_topk_kernel<true>, rows, num_sms, &grid);
+    cudaError_t e = prepare(stream_topk_kernel<true>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
+    const size_t grid = rows < static_cast<size_t>(num_sms) ? rows : static_cast<size_t>(num_sms);
     stream_topk_kernel<true><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, nullptr,
         shard_offset, static_cast<unsigned char *>(records), rec_bytes);
@@ -659,10 +895,12 @@ cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows
                                const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                                float *out_probs, int num_sms, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
-    size_t grid = 0;
-    cudaError_t e = grid_for(shard_merge_kernel, rows, num_sms, &grid);
+    cudaError_t e = prepare(shard_merge_kernel, sizeof(MergeSmem));
     if (e != cudaSuccess) return e;
-    shard_merge_kernel<<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
+    size_t grid = (rows + kMergeWarps - 1) / kMergeWarps;
+    const size_t cap = static_cast<size_t>(num_sms) * 2;
+    if (grid > cap) grid = cap;
+    shard_merge_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem), stream>>>(
         static_cast<const unsigned char *>(records), n_shards, rows, rec_bytes, p, out_ids,
         out_status, out_probs);
     return cudaGetLastError();
