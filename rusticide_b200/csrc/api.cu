@@ -99,8 +99,7 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
                         (!cp.topk_active && vocab <= rsc::kSmallCap));
     cudaError_t e;
     if (small) {
-        e = cudaMemsetAsync(s->large_count, 0, sizeof(uint32_t), stream);
-        if (e != cudaSuccess) return RSC_ERR_CUDA;
+        // large_count is zero here: the draining kernel resets it.
         e = rsc::launch_stream_topk(logits, rows, v, row_stride, cp, ids, status, probs,
                                     s->large_rows, s->large_count, s->num_sms, stream);
         ++s->launches;
@@ -169,7 +168,8 @@ rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab, rsc
     if (slots > s->max_rows) slots = s->max_rows;
     s->large_slots = static_cast<uint32_t>(slots);
     if (e == cudaSuccess) e = cudaMalloc(&s->large_rows, s->max_rows * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMalloc(&s->large_count, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->large_count, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(s->large_count, 0, 2 * sizeof(uint32_t));
     if (e == cudaSuccess)
         e = cudaMalloc(&s->scratch, static_cast<size_t>(s->large_slots) * 4u * s->max_vocab *
                                         sizeof(uint32_t));

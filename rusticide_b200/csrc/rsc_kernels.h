@@ -12,7 +12,7 @@ namespace rsc {
 // Survivor sets up to this size are finished in shared memory by the
 // streaming kernel; larger ones (top-k disabled on a wide row, or ties)
 // go to the large-survivor kernel.
-constexpr uint32_t kSmallCap = 1024;
+constexpr uint32_t kSmallCap = 512;
 // Largest top_k the streaming kernel takes; larger k go to the large kernel.
 constexpr uint32_t kSmallTopK = kSmallCap / 4;
 
@@ -28,12 +28,14 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                uint32_t *large_count, int num_sms, cudaStream_t stream);
 
 // Large-survivor kernel. With large_rows == nullptr it processes rows
-// [0, rows); otherwise the rows listed in large_rows[0 .. *large_count).
+// [0, rows); otherwise the rows listed in large_rows[0 .. large_count[0]),
+// launched as a programmatic dependent of the streaming kernel, and it resets
+// large_count[0..1] to zero when done.
 // Scratch: `slots` regions of 4 * vocab uint32 each.
 cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, const uint32_t *large_rows,
-                         const uint32_t *large_count, uint32_t *scratch, uint32_t slots,
+                         uint32_t *large_count, uint32_t *scratch, uint32_t slots,
                          cudaStream_t stream);
 
 // Vocab-sharded record: this header, then uint32 key[k + RSC_SHARD_TIE_CAP]

@@ -363,17 +363,35 @@ __global__ void __launch_bounds__(kThreads)
 large_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab, size_t row_stride,
              CallParams cp, uint32_t *__restrict__ out_ids, int32_t *__restrict__ out_status,
              float *__restrict__ out_probs, const uint32_t *__restrict__ large_rows,
-             const uint32_t *__restrict__ large_count, uint32_t *__restrict__ scratch) {
+             uint32_t *large_count, uint32_t *__restrict__ scratch) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     LargeSmem &sm = *reinterpret_cast<LargeSmem *>(smem_raw);
     load_exp_table(sm.exp_tab);
     __syncthreads();
-    const size_t count = large_rows ? static_cast<size_t>(*large_count) : rows;
+    // In list mode this grid is launched as a programmatic dependent of the
+    // streaming kernel: wait until that grid has completed and its writes
+    // (the list of overflowing rows) are visible.
+    if (large_rows) asm volatile("griddepcontrol.wait;" ::: "memory");
+    const size_t count = large_rows ? static_cast<size_t>(large_count[0]) : rows;
     uint32_t *my_scratch = scratch + static_cast<size_t>(blockIdx.x) * 4u * vocab;
     for (size_t w = blockIdx.x; w < count; w += gridDim.x) {
         const size_t row = large_rows ? large_rows[w] : w;
         RowView rv{logits + row * row_stride, vocab, cp.scale, cp.mode == kModeSampleWithTemp};
         large_row(cp, rv, row, my_scratch, out_ids, out_status, out_probs, sm);
+    }
+    if (large_rows) {
+        // The last CTA to leave resets the list counter (word 0) and the exit
+        // counter (word 1) for the next call; every CTA read word 0 before
+        // counting itself out.
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(&large_count[1], 1u) == gridDim.x - 1) {
+                large_count[0] = 0;
+                large_count[1] = 0;
+                __threadfence();
+            }
+        }
     }
 }
 
@@ -382,7 +400,7 @@ large_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab, size
 cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, const uint32_t *large_rows,
-                         const uint32_t *large_count, uint32_t *scratch, uint32_t slots,
+                         uint32_t *large_count, uint32_t *scratch, uint32_t slots,
                          cudaStream_t stream) {
     if (rows == 0 || slots == 0) return cudaSuccess;
     const size_t smem = sizeof(LargeSmem);
@@ -391,10 +409,26 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
     if (e != cudaSuccess) return e;
     size_t grid = slots;
     if (grid > rows) grid = rows;
-    large_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(
-        logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
-        large_count, scratch);
-    return cudaGetLastError();
+    if (!large_rows) {
+        large_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(
+            logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
+            large_count, scratch);
+        return cudaGetLastError();
+    }
+    // List mode: a programmatic dependent launch, so that this grid's launch
+    // overlaps the tail of the streaming kernel that fills the list.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, large_kernel, logits, rows, vocab, row_stride, p, out_ids,
+                              out_status, out_probs, large_rows, large_count, scratch);
 }
 
 }  // namespace rsc

@@ -2,7 +2,7 @@
 // (crates/rusticide-sampling/src/sampler.rs:44-54) for rows whose surviving
 // candidate set is small, which is every row once top-k is on.
 //
-// One HBM pass per row, one CTA per SM, three warp roles:
+// One HBM pass per row, three CTAs per SM, each with three warp roles:
 //
 //  producer (1 warp, one lane): keeps a ring of kStages shared-memory stages
 //    filled with 1-D TMA bulk copies (no multicast) of kChunk logits, running
@@ -42,11 +42,11 @@ constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kFinisherWarp = kConsumerWarps + 1;
 constexpr int kThreads = (kConsumerWarps + 2) * 32;
 constexpr uint32_t kChunk = 4096;     // logits per stage (16 KiB)
-constexpr uint32_t kStages = 8;       // 128 KiB of copies in flight per SM
+constexpr uint32_t kStages = 3;       // 48 KiB in flight per CTA
+constexpr int kCtasPerSm = 3;         // three row pipelines per SM: 144 KiB in flight
 constexpr uint32_t kCap = kSmallCap;  // candidate list capacity
 constexpr uint32_t kCompactAt = kCap / 2;
 constexpr int kBarConsumers = 1;      // named barrier of the consumer warps
-constexpr uint32_t kRefresh = 4;      // chunks between bound refreshes (and consumer barriers)
 static_assert(kSmallTopK <= 8 * 32, "tau uses the t-th of 32 lane maxima per warp, t = ceil(k/8)");
 static_assert(kSmallTopK <= kCompactAt / 2, "the list must hold k plus a chunk's new candidates");
 
@@ -57,9 +57,14 @@ struct CandList {
     uint32_t idx[kCap];
 };
 
+// Lists up to this size are ordered by ranks (each lane counts, for its few
+// entries, the entries that precede them) instead of radix select and sorts.
+constexpr uint32_t kRankMax = 128;
+
 // Workspace of one finishing warp.
 struct FinishWork {
-    unsigned long long items[kCap];
+    unsigned long long items[kCap];   // (~key, idx): value desc, index asc
+    unsigned long long items2[kCap];  // (idx, key): index asc
     float vals[kCap];
     uint32_t hist[256];
     uint32_t sel[2];
@@ -126,22 +131,21 @@ __device__ __forceinline__ bool consumers_any(bool p) {
     return r != 0;
 }
 
-// Appends the logits of a float4 group that pass `tau` (one shared atomic per
-// lane that has any). Returns true if the list grew past `mark`.
-__device__ __forceinline__ bool append_group(CandList &L, uint32_t *count, uint32_t *overflow,
-                                             float tau, float v0, float v1, float v2, float v3,
-                                             uint32_t i0, uint32_t mark) {
-    const uint32_t c = (v0 >= tau ? 1u : 0u) + (v1 >= tau ? 1u : 0u) + (v2 >= tau ? 1u : 0u) +
-                       (v3 >= tau ? 1u : 0u);
-    if (!c) return false;
-    uint32_t pos = atomicAdd(count, c);
-    const float v[4] = {v0, v1, v2, v3};
+// Appends the logits of this thread's chunk slice whose bit is set in `m`
+// (bit 4*jj + e: element e of float4 jj, global index i0 + 4*kConsumers*jj + e).
+// One shared atomic per thread that has any. Returns true if the list grew
+// past `mark`.
+template <int N>
+__device__ __forceinline__ bool append_mask(CandList &L, uint32_t *count, uint32_t *overflow,
+                                            uint32_t m, const float (&v)[N], uint32_t i0,
+                                            uint32_t mark) {
+    uint32_t pos = atomicAdd(count, static_cast<uint32_t>(__popc(m)));
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        if (v[q] >= tau) {
+    for (int e = 0; e < N; ++e) {  // unrolled: v stays in registers
+        if ((m >> e) & 1u) {
             if (pos < kCap) {
-                L.key[pos] = total_key(v[q]);
-                L.idx[pos] = i0 + q;
+                L.key[pos] = total_key(v[e]);
+                L.idx[pos] = i0 + static_cast<uint32_t>(e >> 2) * (4 * kConsumers) + (e & 3);
             } else {
                 *overflow = 1;
             }
@@ -180,6 +184,20 @@ __device__ __forceinline__ bool append_candidate(CandList &L, uint32_t *count, u
 __device__ __forceinline__ void post_warp_bound(StreamSmem &sm, float lmax, uint32_t t, int cw,
                                                 uint32_t par) {
     const int lane = threadIdx.x & 31;
+    if (t <= 8) {
+        // Small t: t-1 rounds of "remove one lane holding the maximum", then
+        // the maximum of the rest, with hardware warp max reductions on
+        // total-order keys (-inf maps above 0, the removed value).
+        uint32_t key = total_key(lmax);
+        for (uint32_t i = 1; i < t; ++i) {
+            const uint32_t m = __reduce_max_sync(0xffffffffu, key);
+            const uint32_t b = __ballot_sync(0xffffffffu, key == m);
+            if (lane == __ffs(b) - 1) key = 0u;
+        }
+        const uint32_t m = __reduce_max_sync(0xffffffffu, key);
+        if (lane == 0) sm.warp_tau[par][cw] = key_to_float(m);
+        return;
+    }
     float m = lmax;
 #pragma unroll
     for (int k = 2; k <= 32; k <<= 1) {
@@ -332,24 +350,57 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
                             const uint32_t *cidx, uint32_t count, const CallParams &cp, size_t row,
                             uint32_t *out_ids, int32_t *out_status, float *out_probs) {
     const int lane = threadIdx.x & 31;
-    // Exact top-k threshold (candidates.rs:38-43). With fewer than k
-    // candidates every candidate survives (the k-th largest is then -inf or
-    // below, which keeps every value that is not -inf).
-    float thr = kNegInf;
-    if (cp.topk_active && count >= cp.top_k) {
-        const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
-            count, cp.top_k, [&](uint32_t i) { return ckey[i]; }, fw.hist, fw.sel);
-        thr = key_to_float(kth);
-    }
     const bool topp = cp.topp_active;
-    uint32_t n = gather_survivors(fw, ckey, cidx, count,
-                                  [&](uint32_t key, uint32_t idx, unsigned long long *it) {
-                                      *it = topp ? pack_key_index(~key, idx) : pack_key_index(idx, key);
-                                      return survives(key_to_float(key), thr);
-                                  });
-    uint32_t n64 = pow2_at_least(n);
-    for (uint32_t i = n + lane; i < n64; i += 32) fw.items[i] = ~0ull;
-    group_bitonic_sort<32, SyncWarp>(fw.items, n64);
+    // Exact top-k threshold (candidates.rs:38-43) and the survivors of the
+    // keep test (:44-51) in (value desc, index asc) order. With fewer than k
+    // candidates every candidate survives (the k-th largest is then -inf or
+    // below, which keeps every value that is not -inf). The survivors are a
+    // prefix of that order: the keys at or above the threshold's, then -0.0
+    // after a +0.0 threshold (IEEE -0.0 < +0.0 is false).
+    float thr = kNegInf;
+    uint32_t n;
+    if (count <= kRankMax) {
+        constexpr int kPer = kRankMax / 32;
+        uint32_t mk[kPer], mi[kPer], rank[kPer];
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const uint32_t i = lane + 32 * q;
+            mk[q] = i < count ? ckey[i] : 0u;
+            mi[q] = i < count ? cidx[i] : ~0u;
+            rank[q] = 0;
+        }
+        for (uint32_t j = 0; j < count; ++j) {
+            const uint32_t kj = ckey[j], ij = cidx[j];
+#pragma unroll
+            for (int q = 0; q < kPer; ++q)
+                rank[q] += (kj > mk[q] || (kj == mk[q] && ij < mi[q])) ? 1u : 0u;
+        }
+#pragma unroll
+        for (int q = 0; q < kPer; ++q)
+            if (lane + 32 * q < count) fw.items[rank[q]] = pack_key_index(~mk[q], mi[q]);
+        __syncwarp();
+        if (cp.topk_active && count >= cp.top_k)
+            thr = key_to_float(~static_cast<uint32_t>(fw.items[cp.top_k - 1] >> 32));
+        uint32_t s = 0;
+#pragma unroll
+        for (int q = 0; q < kPer; ++q)
+            s += (lane + 32 * q < count && survives(key_to_float(mk[q]), thr)) ? 1u : 0u;
+        n = __reduce_add_sync(0xffffffffu, s);
+    } else {
+        if (cp.topk_active && count >= cp.top_k) {
+            const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
+                count, cp.top_k, [&](uint32_t i) { return ckey[i]; }, fw.hist, fw.sel);
+            thr = key_to_float(kth);
+        }
+        n = gather_survivors(fw, ckey, cidx, count,
+                             [&](uint32_t key, uint32_t idx, unsigned long long *it) {
+                                 *it = pack_key_index(~key, idx);
+                                 return survives(key_to_float(key), thr);
+                             });
+        const uint32_t n64 = pow2_at_least(n);
+        for (uint32_t i = n + lane; i < n64; i += 32) fw.items[i] = ~0ull;
+        group_bitonic_sort<32, SyncWarp>(fw.items, n64);
+    }
 
     if (topp && n > 0) {
         // Candidates::top_p (candidates.rs:55-78): items are (~key, idx)
@@ -369,27 +420,52 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
             cut = at < n ? at + 1 : n;
         }
         n = __shfl_sync(0xffffffffu, cut, 0);
-        // Re-key the kept prefix by index and sort it back to index order.
+    }
+
+    // The kept set back in index order (Candidates::top_p re-sorts by index,
+    // candidates.rs:77), as (idx, key) in fw.items2.
+    if (n <= kRankMax) {
+        constexpr int kPer = kRankMax / 32;
+        uint32_t mi[kPer], mk[kPer], rank[kPer];
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const uint32_t i = lane + 32 * q;
+            const unsigned long long x = i < n ? fw.items[i] : ~0ull;
+            mi[q] = static_cast<uint32_t>(x);
+            mk[q] = ~static_cast<uint32_t>(x >> 32);
+            rank[q] = 0;
+        }
+        for (uint32_t j = 0; j < n; ++j) {
+            const uint32_t ij = static_cast<uint32_t>(fw.items[j]);
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) rank[q] += ij < mi[q] ? 1u : 0u;
+        }
+#pragma unroll
+        for (int q = 0; q < kPer; ++q)
+            if (lane + 32 * q < n) fw.items2[rank[q]] = pack_key_index(mi[q], mk[q]);
+        __syncwarp();
+    } else {
+        const uint32_t n64 = pow2_at_least(n);
         for (uint32_t i = lane; i < n64; i += 32) {
             const unsigned long long x = fw.items[i];
-            fw.items[i] = i < n ? pack_key_index(static_cast<uint32_t>(x), ~static_cast<uint32_t>(x >> 32))
-                                : ~0ull;
+            fw.items2[i] = i < n ? pack_key_index(static_cast<uint32_t>(x), ~static_cast<uint32_t>(x >> 32))
+                                 : ~0ull;
         }
-        group_bitonic_sort<32, SyncWarp>(fw.items, n64);
+        group_bitonic_sort<32, SyncWarp>(fw.items2, n64);
     }
 
     if (cp.out_nsurv && lane == 0) cp.out_nsurv[row] = n;
     if (cp.out_surv) {
         const uint32_t m = min(n, cp.surv_cap);
         for (uint32_t i = lane; i < m; i += 32)
-            cp.out_surv[row * cp.surv_cap + i] = static_cast<uint32_t>(fw.items[i] >> 32);
+            cp.out_surv[row * cp.surv_cap + i] = static_cast<uint32_t>(fw.items2[i] >> 32);
     }
 
     // softmax (filters.rs:5-15) over the survivors in index order.
     float mx = kNegInf;
     unsigned long long amax = 0;
     for (uint32_t i = lane; i < n; i += 32) {
-        const uint32_t key = static_cast<uint32_t>(fw.items[i]);
+        const uint32_t key = static_cast<uint32_t>(fw.items2[i]);
         mx = fmaxf(mx, key_to_float(key));
         const unsigned long long c = pack_key_index(key, i);
         amax = c > amax ? c : amax;
@@ -401,7 +477,7 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
         amax = a > amax ? a : amax;
     }
     for (uint32_t i = lane; i < n; i += 32)
-        fw.vals[i] = expf_ref(__fsub_rn(key_to_float(static_cast<uint32_t>(fw.items[i])), mx), tab);
+        fw.vals[i] = expf_ref(__fsub_rn(key_to_float(static_cast<uint32_t>(fw.items2[i])), mx), tab);
     __syncwarp();
     float sum = 0.0f;
     if (lane == 0) sum = chain_sum(fw.vals, n, -0.0f);  // <f32 as Sum>::sum folds from -0.0
@@ -433,7 +509,7 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
                 if (fabsf(r - hi) < 1e-6f || fabsf(r - lo) < 1e-6f)
                     status |= RSC_ROW_FLAG_DRAW_NEAR_BOUNDARY;
             }
-            token = static_cast<uint32_t>(fw.items[pos] >> 32);
+            token = static_cast<uint32_t>(fw.items2[pos] >> 32);
             prob = fw.vals[pos];
         }
         out_ids[row] = token;
@@ -491,7 +567,7 @@ __device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t
 // --- the streaming kernel -------------------------------------------------------
 
 template <bool kRecord>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
 stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab,
                    size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs,
@@ -516,6 +592,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         fence_barrier_init();
     }
     __syncthreads();  // the last block-wide barrier: the roles split here
+    // The kernel that drains overflowing rows may start launching now; it
+    // waits for this grid's completion before reading the list.
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;");
 
     if (warp == kProducerWarp) {
         if (lane != 0) return;
@@ -697,22 +776,32 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage s released by this warp
             ++consumed;
+            float v[4 * kPerThread];
+            uint32_t m = 0;
 #pragma unroll
             for (uint32_t jj = 0; jj < kPerThread; ++jj) {
-                const uint32_t q = threadIdx.x + jj * kConsumers;
-                const float v0 = __fmul_rn(f[jj].x, scale), v1 = __fmul_rn(f[jj].y, scale);
-                const float v2 = __fmul_rn(f[jj].z, scale), v3 = __fmul_rn(f[jj].w, scale);
-                stats(v0);
-                stats(v1);
-                stats(v2);
-                stats(v3);
-                lmax = fmaxf(fmaxf(lmax, fmaxf(v0, v1)), fmaxf(v2, v3));
-                mark |= append_group(L, count, ovf, tau, v0, v1, v2, v3, base_idx + 4 * q, kCompactAt);
+                v[4 * jj + 0] = __fmul_rn(f[jj].x, scale);
+                v[4 * jj + 1] = __fmul_rn(f[jj].y, scale);
+                v[4 * jj + 2] = __fmul_rn(f[jj].z, scale);
+                v[4 * jj + 3] = __fmul_rn(f[jj].w, scale);
             }
+#pragma unroll
+            for (uint32_t e = 0; e < 4 * kPerThread; ++e) {
+                stats(v[e]);
+                m |= (v[e] >= tau ? 1u : 0u) << e;
+            }
+            float cm = v[0];
+#pragma unroll
+            for (uint32_t e = 1; e < 4 * kPerThread; ++e) cm = fmaxf(cm, v[e]);
+            lmax = fmaxf(lmax, cm);
+            if (m) mark |= append_mask(L, count, ovf, m, v, base_idx + 4 * threadIdx.x, kCompactAt);
             const bool last = c + 1 == g.nchunks;
-            if (!last && (c + 1) % kRefresh != 0) continue;
+            // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
+            const uint32_t done = c + 1;
+            const bool refresh = last || (done < 8 ? (done & (done - 1)) == 0 && done > 1 : done % 8 == 0);
+            if (!refresh) continue;
             if (t_bound) post_warp_bound(sm, lmax, t_bound, cw, par);
-            // One barrier every kRefresh chunks: settles the list, publishes
+            // One barrier per refresh: settles the list, publishes
             // the bounds, and raises the rare events (a failed wait, a long
             // list).
             const bool want_compact = mark && cp.topk_active && !last;
@@ -870,7 +959,8 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
     if (rows == 0) return cudaSuccess;
     cudaError_t e = prepare(stream_topk_kernel<false>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
-    const size_t grid = rows < static_cast<size_t>(num_sms) ? rows : static_cast<size_t>(num_sms);
+    const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
+    const size_t grid = rows < ctas ? rows : ctas;
     stream_topk_kernel<false><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
         large_count, 0u, nullptr, 0);
@@ -884,7 +974,8 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
     if (rows == 0) return cudaSuccess;
     cudaError_t e = prepare(stream_topk_kernel<true>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
-    const size_t grid = rows < static_cast<size_t>(num_sms) ? rows : static_cast<size_t>(num_sms);
+    const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
+    const size_t grid = rows < ctas ? rows : ctas;
     stream_topk_kernel<true><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, nullptr,
         shard_offset, static_cast<unsigned char *>(records), rec_bytes);
