@@ -749,15 +749,16 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             if (c == 0 && t_bound) {
                 // First chunk: lane maxima before filtering, so that tau is
                 // already high for this chunk's own logits.
+                float cmr = kNegInf;
 #pragma unroll
                 for (uint32_t jj = 0; jj < kChunk / 4 / kConsumers; ++jj) {
                     const uint32_t q = threadIdx.x + jj * kConsumers;
                     if (4 * q < len) {
                         const float4 f = r4[q];
-                        lmax = fmaxf(fmaxf(lmax, fmaxf(__fmul_rn(f.x, scale), __fmul_rn(f.y, scale))),
-                                     fmaxf(__fmul_rn(f.z, scale), __fmul_rn(f.w, scale)));
+                        cmr = fmaxf(fmaxf(cmr, fmaxf(f.x, f.y)), fmaxf(f.z, f.w));
                     }
                 }
+                lmax = fmaxf(lmax, __fmul_rn(cmr, scale));
                 post_warp_bound(sm, lmax, t_bound, cw, par);
                 if (consumers_any(!got)) {
                     stop = true;
@@ -776,25 +777,33 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage s released by this warp
             ++consumed;
-            float v[4 * kPerThread];
-            uint32_t m = 0;
+            // x -> fl(x * scale) is non-decreasing for a finite scale > 0, so
+            // the largest scaled value of this thread's slice is the scaled
+            // largest raw value: one max per logit decides whether the slice
+            // holds a candidate at all (fmaxf skips NaN, which reads as -inf).
+            float cmr = f[0].x;
 #pragma unroll
-            for (uint32_t jj = 0; jj < kPerThread; ++jj) {
-                v[4 * jj + 0] = __fmul_rn(f[jj].x, scale);
-                v[4 * jj + 1] = __fmul_rn(f[jj].y, scale);
-                v[4 * jj + 2] = __fmul_rn(f[jj].z, scale);
-                v[4 * jj + 3] = __fmul_rn(f[jj].w, scale);
-            }
-#pragma unroll
-            for (uint32_t e = 0; e < 4 * kPerThread; ++e) {
-                stats(v[e]);
-                m |= (v[e] >= tau ? 1u : 0u) << e;
-            }
-            float cm = v[0];
-#pragma unroll
-            for (uint32_t e = 1; e < 4 * kPerThread; ++e) cm = fmaxf(cm, v[e]);
+            for (uint32_t jj = 0; jj < kPerThread; ++jj)
+                cmr = fmaxf(fmaxf(cmr, fmaxf(f[jj].x, f[jj].y)), fmaxf(f[jj].z, f[jj].w));
+            const float cm = __fmul_rn(cmr, scale);
             lmax = fmaxf(lmax, cm);
-            if (m) mark |= append_mask(L, count, ovf, m, v, base_idx + 4 * threadIdx.x, kCompactAt);
+            if (kRecord || cm >= tau) {
+                float v[4 * kPerThread];
+                uint32_t m = 0;
+#pragma unroll
+                for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                    v[4 * jj + 0] = __fmul_rn(f[jj].x, scale);
+                    v[4 * jj + 1] = __fmul_rn(f[jj].y, scale);
+                    v[4 * jj + 2] = __fmul_rn(f[jj].z, scale);
+                    v[4 * jj + 3] = __fmul_rn(f[jj].w, scale);
+                }
+#pragma unroll
+                for (uint32_t e = 0; e < 4 * kPerThread; ++e) {
+                    stats(v[e]);
+                    m |= (v[e] >= tau ? 1u : 0u) << e;
+                }
+                if (m) mark |= append_mask(L, count, ovf, m, v, base_idx + 4 * threadIdx.x, kCompactAt);
+            }
             const bool last = c + 1 == g.nchunks;
             // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
             const uint32_t done = c + 1;
