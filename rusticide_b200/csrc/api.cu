@@ -21,8 +21,11 @@ struct rsc_sampler {
     int num_sms = 0;
     uint32_t large_slots = 0;
     uint32_t *large_rows = nullptr;   // [max_rows]
-    uint32_t *large_count = nullptr;  // [1]
+    uint32_t *large_count = nullptr;  // [2]: list length, drain exit count
     uint32_t *scratch = nullptr;      // [large_slots][4 * max_vocab]
+    size_t max_units = 0;             // row segments of the streaming kernel
+    void *seg_records = nullptr;      // [max_units] records of split_record_bytes(splits >= 2)
+    uint32_t *row_arrivals = nullptr; // [max_rows], zero between calls
     // Device staging of rsc_pick_host.
     float *stage_logits = nullptr;
     float *stage_uniforms = nullptr;
@@ -100,8 +103,10 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
     cudaError_t e;
     if (small) {
         // large_count is zero here: the draining kernel resets it.
+        const uint32_t splits = rsc::stream_splits(rows, v, cp.top_k, s->num_sms, s->max_units);
         e = rsc::launch_stream_topk(logits, rows, v, row_stride, cp, ids, status, probs,
-                                    s->large_rows, s->large_count, s->num_sms, stream);
+                                    s->large_rows, s->large_count, splits, s->seg_records,
+                                    s->row_arrivals, s->num_sms, stream);
         ++s->launches;
         if (e != cudaSuccess) return RSC_ERR_CUDA;
         e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->large_rows,
@@ -173,6 +178,13 @@ rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab, rsc
     if (e == cudaSuccess)
         e = cudaMalloc(&s->scratch, static_cast<size_t>(s->large_slots) * 4u * s->max_vocab *
                                         sizeof(uint32_t));
+    // Segment records: up to 4 segments per row, and up to kStreamMaxSplits
+    // per row for batches smaller than the GPU.
+    s->max_units = 4 * s->max_rows + rsc::kStreamMaxSplits * static_cast<size_t>(s->num_sms) * 4;
+    if (e == cudaSuccess)
+        e = cudaMalloc(&s->seg_records, s->max_units * rsc::split_record_bytes(2));
+    if (e == cudaSuccess) e = cudaMalloc(&s->row_arrivals, s->max_rows * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(s->row_arrivals, 0, s->max_rows * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMalloc(&s->stage_logits, s->max_rows * s->max_vocab * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&s->stage_uniforms, s->max_rows * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&s->stage_ids, s->max_rows * sizeof(uint32_t));
@@ -195,6 +207,8 @@ rsc_status rsc_sampler_destroy(rsc_sampler *s) {
     cudaFree(s->large_rows);
     cudaFree(s->large_count);
     cudaFree(s->scratch);
+    cudaFree(s->seg_records);
+    cudaFree(s->row_arrivals);
     cudaFree(s->stage_logits);
     cudaFree(s->stage_uniforms);
     cudaFree(s->stage_ids);

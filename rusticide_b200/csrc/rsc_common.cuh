@@ -236,14 +236,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// One potentially blocking test of the barrier: a waiting thread is suspended
+// (up to 100 us) rather than spinning, so it takes no issue slots from the
+// warps that are working.
 __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(addr), "r"(parity)
+        : "r"(addr), "r"(parity), "r"(100000u)
         : "memory");
     return done != 0;
 }
@@ -255,9 +258,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try(addr, parity)) return true;
     const unsigned long long t0 = global_ns();
     while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 256; ++i)
-            if (mbar_try(addr, parity)) return true;
+        if (mbar_try(addr, parity)) return true;
         if (global_ns() - t0 > kWaitLimitNs) return false;
     }
 }

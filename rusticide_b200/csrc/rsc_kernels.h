@@ -20,12 +20,30 @@ cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size
                           uint32_t *out_ids, int32_t *out_status, int num_sms,
                           cudaStream_t stream);
 
+// Most segments a row is cut into by the streaming kernel.
+constexpr uint32_t kStreamMaxSplits = 16;
+
+// Bytes of one segment record when rows are split `splits` ways (kSmallCap /
+// splits entries).
+size_t split_record_bytes(uint32_t splits);
+
+// Number of segments per row that spreads `rows` best over the streaming
+// kernel's CTAs (rows * result <= max_units, and the segments' merged
+// records fit one candidate list).
+uint32_t stream_splits(size_t rows, uint32_t vocab, uint32_t top_k, int num_sms,
+                       size_t max_units);
+
 // Streaming top-k kernel for rows whose survivors fit kSmallCap. Rows that
-// overflow are appended to large_rows[*large_count].
+// overflow are appended to large_rows[large_count[0]]. With splits > 1 each
+// row is cut into that many segments; seg_records (rows * splits records of
+// shard_record_bytes(top_k)) and row_arrivals (rows counters, zero on entry
+// and on exit) carry the segments' candidates to the segment that finishes
+// the row.
 cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                size_t row_stride, const CallParams &p, uint32_t *out_ids,
                                int32_t *out_status, float *out_probs, uint32_t *large_rows,
-                               uint32_t *large_count, int num_sms, cudaStream_t stream);
+                               uint32_t *large_count, uint32_t splits, void *seg_records,
+                               uint32_t *row_arrivals, int num_sms, cudaStream_t stream);
 
 // Large-survivor kernel. With large_rows == nullptr it processes rows
 // [0, rows); otherwise the rows listed in large_rows[0 .. large_count[0]),
@@ -49,7 +67,8 @@ struct ShardRecordHeader {
     uint32_t n_dropped;  // entries at or above the local threshold that did not fit
     uint32_t last_key;   // key of the last entry
     uint32_t flags;      // 0 ok; 1 candidate list overflow; 2 a device wait gave up
-    uint32_t reserved;
+    float tau;           // a lower bound of the part's k-th largest scaled value; every
+                         // value at or above it is an entry unless n_dropped > 0
 };
 static_assert(sizeof(ShardRecordHeader) == 32, "record header layout");
 

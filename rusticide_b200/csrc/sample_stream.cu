@@ -47,6 +47,7 @@ constexpr int kCtasPerSm = 3;         // three row pipelines per SM: 144 KiB in 
 constexpr uint32_t kCap = kSmallCap;  // candidate list capacity
 constexpr uint32_t kCompactAt = kCap / 2;
 constexpr int kBarConsumers = 1;      // named barrier of the consumer warps
+constexpr uint32_t kMaxSplits = kStreamMaxSplits;
 static_assert(kSmallTopK <= 8 * 32, "tau uses the t-th of 32 lane maxima per warp, t = ceil(k/8)");
 static_assert(kSmallTopK <= kCompactAt / 2, "the list must hold k plus a chunk's new candidates");
 
@@ -360,25 +361,47 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
     float thr = kNegInf;
     uint32_t n;
     if (count <= kRankMax) {
+        // (key, ~idx) as one 64-bit word: entry j precedes entry i in the
+        // (value desc, index asc) order exactly when its word is larger, so a
+        // rank is a count of larger words (branch-free compares).
         constexpr int kPer = kRankMax / 32;
-        uint32_t mk[kPer], mi[kPer], rank[kPer];
+        for (uint32_t i = lane; i < count; i += 32) fw.items2[i] = pack_key_index(ckey[i], ~cidx[i]);
+        __syncwarp();
+        unsigned long long mine[kPer];
+        uint32_t rank[kPer];
 #pragma unroll
         for (int q = 0; q < kPer; ++q) {
             const uint32_t i = lane + 32 * q;
-            mk[q] = i < count ? ckey[i] : 0u;
-            mi[q] = i < count ? cidx[i] : ~0u;
+            mine[q] = i < count ? fw.items2[i] : ~0ull;
             rank[q] = 0;
         }
-        for (uint32_t j = 0; j < count; ++j) {
-            const uint32_t kj = ckey[j], ij = cidx[j];
+        uint32_t j = 0;
+        for (; j + 4 <= count; j += 4) {
+            unsigned long long w[4];
 #pragma unroll
-            for (int q = 0; q < kPer; ++q)
-                rank[q] += (kj > mk[q] || (kj == mk[q] && ij < mi[q])) ? 1u : 0u;
+            for (int e = 0; e < 4; ++e) w[e] = fw.items2[j + e];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+#pragma unroll
+                for (int q = 0; q < kPer; ++q) rank[q] += w[e] > mine[q] ? 1u : 0u;
+        }
+        for (; j < count; ++j) {
+            const unsigned long long w = fw.items2[j];
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) rank[q] += w > mine[q] ? 1u : 0u;
         }
 #pragma unroll
-        for (int q = 0; q < kPer; ++q)
-            if (lane + 32 * q < count) fw.items[rank[q]] = pack_key_index(~mk[q], mi[q]);
+        for (int q = 0; q < kPer; ++q) {
+            if (lane + 32 * q < count) {
+                const uint32_t key = static_cast<uint32_t>(mine[q] >> 32);
+                const uint32_t idx = ~static_cast<uint32_t>(mine[q]);
+                fw.items[rank[q]] = pack_key_index(~key, idx);
+            }
+        }
         __syncwarp();
+        uint32_t mk[kPer];
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) mk[q] = static_cast<uint32_t>(mine[q] >> 32);
         if (cp.topk_active && count >= cp.top_k)
             thr = key_to_float(~static_cast<uint32_t>(fw.items[cp.top_k - 1] >> 32));
         uint32_t s = 0;
@@ -435,7 +458,17 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
             mk[q] = ~static_cast<uint32_t>(x >> 32);
             rank[q] = 0;
         }
-        for (uint32_t j = 0; j < n; ++j) {
+        uint32_t j = 0;
+        for (; j + 4 <= n; j += 4) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w[e] = static_cast<uint32_t>(fw.items[j + e]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+#pragma unroll
+                for (int q = 0; q < kPer; ++q) rank[q] += w[e] < mi[q] ? 1u : 0u;
+        }
+        for (; j < n; ++j) {
             const uint32_t ij = static_cast<uint32_t>(fw.items[j]);
 #pragma unroll
             for (int q = 0; q < kPer; ++q) rank[q] += ij < mi[q] ? 1u : 0u;
@@ -519,14 +552,38 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
     __syncwarp();
 }
 
-// Shard record of the vocab-sharded mode (one warp): every candidate at or
-// above the shard's k-th largest key, sorted (key desc, index asc), capped at
-// k + RSC_SHARD_TIE_CAP entries, plus the shard's row statistics.
+// Record of one part of a row (a vocab shard, or a segment of a split row),
+// written by one warp: the part's candidates that can reach the row's k-th
+// largest value, at most `cap_entries` of them, and the part's row statistics.
+// If the pre-cut list fits, it is written as it is (every entry is at or above
+// `tau`, a lower bound of the part's k-th largest value). Otherwise only the
+// entries at or above the part's own k-th largest key are kept, sorted (key
+// desc, index asc) and capped, and the number dropped is recorded.
 __device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t *cidx,
                             uint32_t count, const CallParams &cp, float M, float S, uint32_t nfin,
-                            unsigned char *rec) {
+                            unsigned char *rec, uint32_t cap_entries, float tau) {
     const int lane = threadIdx.x & 31;
-    const uint32_t cap_entries = cp.top_k + RSC_SHARD_TIE_CAP;
+    ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+    uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
+    uint32_t *ridx = rkey + cap_entries;
+    if (count <= cap_entries) {
+        for (uint32_t i = lane; i < count; i += 32) {
+            rkey[i] = ckey[i];
+            ridx[i] = cidx[i];
+        }
+        if (lane == 0) {
+            h->max_scaled = M;
+            h->sum_exp = S;
+            h->n_finite = nfin;
+            h->n_cand = count;
+            h->n_dropped = 0;
+            h->last_key = 0;
+            h->flags = 0;
+            h->tau = tau;
+        }
+        __syncwarp();
+        return;
+    }
     uint32_t floor_key = kKeyNegInf + 1u;
     if (count >= cp.top_k) {
         const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
@@ -543,9 +600,6 @@ __device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t
     for (uint32_t i = n + lane; i < n64; i += 32) fw.items[i] = ~0ull;
     group_bitonic_sort<32, SyncWarp>(fw.items, n64);
     const uint32_t nc = min(n, cap_entries);
-    ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
-    uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
-    uint32_t *ridx = rkey + cap_entries;
     for (uint32_t i = lane; i < nc; i += 32) {
         const unsigned long long x = fw.items[i];
         rkey[i] = ~static_cast<uint32_t>(x >> 32);
@@ -559,9 +613,78 @@ __device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t
         h->n_dropped = n - nc;
         h->last_key = nc ? ~static_cast<uint32_t>(fw.items[nc - 1] >> 32) : 0u;
         h->flags = 0;
-        h->reserved = 0;
+        h->tau = key_to_float(floor_key);
     }
     __syncwarp();
+}
+
+// Gathers one row's records from `n` parts (vocab shards or row segments)
+// into the candidate list L (one warp) and returns their number. The entries
+// below the largest of the parts' bounds are dropped on the way: each bound is
+// at most its part's k-th largest value, hence at most the row's. *ok becomes
+// false when the union cannot be trusted: a part overflowed, the union exceeds
+// kCap, or a part dropped tied entries that could reach the row's k-th
+// largest value. Records may come from other CTAs of the same grid, so they
+// are read past L1 (ld.global.cg).
+template <typename RecAt>
+__device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uint32_t n,
+                                  uint32_t cap_entries, const CallParams &cp, bool *ok) {
+    const int lane = threadIdx.x & 31;
+    bool good = true;
+    float tau = -3.402823466e38f;
+    bool any_dropped = false;
+    for (uint32_t s = 0; s < n; ++s) {
+        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(s));
+        if (__ldcg(h + 6)) good = false;
+        tau = fmaxf(tau, __uint_as_float(__ldcg(h + 7)));
+        any_dropped |= __ldcg(h + 4) > 0;
+    }
+    uint32_t count = 0;
+    for (uint32_t s = 0; s < n && good; ++s) {
+        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(s));
+        const uint32_t nc = min(__ldcg(h + 3), cap_entries);
+        const uint32_t *rkey = h + 8;
+        const uint32_t *ridx = rkey + cap_entries;
+        for (uint32_t base = 0; base < nc; base += 32) {
+            const uint32_t i = base + lane;
+            uint32_t key = 0, idx = 0;
+            bool keep = false;
+            if (i < nc) {
+                key = __ldcg(rkey + i);
+                idx = __ldcg(ridx + i);
+                keep = key_to_float(key) >= tau;
+            }
+            const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+            const uint32_t pos = count + __popc(ballot & ((1u << lane) - 1u));
+            if (keep && pos < kCap) {
+                L.key[pos] = key;
+                L.idx[pos] = idx;
+            }
+            count += __popc(ballot);
+        }
+    }
+    if (count > kCap) good = false;
+    __syncwarp();
+    if (good && any_dropped) {
+        uint32_t floor_key = 0u;
+        const bool have_kth = cp.topk_active && count >= cp.top_k;
+        if (have_kth) {
+            const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
+                count, cp.top_k, [&](uint32_t i) { return L.key[i]; }, fw.hist, fw.sel);
+            floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
+        }
+        for (uint32_t s = 0; s < n; ++s) {
+            const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(s));
+            if (__ldcg(h + 4) > 0 && (!have_kth || __ldcg(h + 5) >= floor_key)) good = false;
+        }
+    }
+    *ok = good;
+    return min(count, kCap);
+}
+
+// First chunk of segment `seg` of a row of `nchunks` chunks split `splits` ways.
+__device__ __forceinline__ uint32_t seg_begin(uint32_t nchunks, uint32_t seg, uint32_t splits) {
+    return static_cast<uint32_t>((static_cast<unsigned long long>(nchunks) * seg) / splits);
 }
 
 // --- the streaming kernel -------------------------------------------------------
@@ -572,10 +695,17 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                    size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs,
                    uint32_t *__restrict__ large_rows, uint32_t *__restrict__ large_count,
-                   uint32_t index_offset, unsigned char *__restrict__ records, size_t rec_bytes) {
+                   uint32_t index_offset, unsigned char *__restrict__ records, size_t rec_bytes,
+                   uint32_t splits, unsigned char *__restrict__ seg_records,
+                   uint32_t *__restrict__ row_arrivals) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     StreamSmem &sm = *reinterpret_cast<StreamSmem *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Work units: row r, segment g (unit r * splits + g); a segment is a run
+    // of whole chunks, segment 0 also takes the scalar head, the last segment
+    // the scalar tail.
+    const size_t units = rows * splits;
+    const uint32_t seg_cap = kCap / splits;  // entries of a segment record
 
     load_exp_table(sm.exp_tab);
     if (threadIdx.x == 0) {
@@ -600,9 +730,12 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         if (lane != 0) return;
         uint32_t q = 0;
         bool ok = true;
-        for (size_t row = blockIdx.x; row < rows && ok; row += gridDim.x) {
+        for (size_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const size_t row = u / splits;
+            const uint32_t seg = static_cast<uint32_t>(u % splits);
             const RowGeom g = row_geom(logits, row, row_stride, vocab);
-            for (uint32_t c = 0; c < g.nchunks; ++c) {
+            const uint32_t c1 = seg_begin(g.nchunks, seg + 1, splits);
+            for (uint32_t c = seg_begin(g.nchunks, seg, splits); c < c1; ++c) {
                 const uint32_t s = q % kStages;
                 if (q >= kStages && !mbar_wait(&sm.empty[s], ((q / kStages) - 1u) & 1u)) {
                     atomicExch(&sm.error, 1u);
@@ -628,8 +761,10 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
 
     if (warp == kFinisherWarp) {
         uint32_t j = 0;
-        size_t row = blockIdx.x;
-        for (; row < rows; row += gridDim.x, ++j) {
+        size_t u = blockIdx.x;
+        for (; u < units; u += gridDim.x, ++j) {
+            const size_t row = u / splits;
+            const uint32_t seg = static_cast<uint32_t>(u % splits);
             const uint32_t b = j & 1u;
             const bool got = mbar_wait(&sm.list_full[b], (j >> 1) & 1u);
             if (__any_sync(0xffffffffu, !got)) {
@@ -658,14 +793,50 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     float S = 0.0f;
                     for (int w = 0; w < kConsumerWarps; ++w)
                         if (sm.st_sum[b][w] > 0.0f) S += sm.st_sum[b][w] * __expf(sm.st_max[b][w] - M);
-                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, M, S, nfin, rec);
+                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, M, S, nfin, rec,
+                                cp.top_k + RSC_SHARD_TIE_CAP, sm.tau_final[b]);
                 }
-            } else {
+            } else if (splits == 1) {
                 if (ov) {
                     if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
                 } else {
                     finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, cnt, cp, row,
                                 out_ids, out_status, out_probs);
+                }
+            } else {
+                // One segment of a split row: publish its record, and the
+                // segment that completes the row merges all of them.
+                unsigned char *rec = seg_records + (row * splits + seg) * rec_bytes;
+                if (ov) {
+                    if (lane == 0) {
+                        ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                        h->n_cand = 0;
+                        h->n_dropped = 0;
+                        h->flags = 1;
+                    }
+                } else {
+                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, 0.0f, 0.0f, 0u, rec,
+                                seg_cap, sm.tau_final[b]);
+                }
+                __threadfence();
+                __syncwarp();
+                uint32_t arrived = 0;
+                if (lane == 0) arrived = atomicAdd(&row_arrivals[row], 1u);
+                arrived = __shfl_sync(0xffffffffu, arrived, 0);
+                if (arrived == splits - 1) {
+                    __threadfence();
+                    bool ok = true;
+                    const uint32_t n = merge_records(
+                        sm.list[b], sm.fw,
+                        [&](uint32_t part) { return seg_records + (row * splits + part) * rec_bytes; },
+                        splits, seg_cap, cp, &ok);
+                    if (!ok) {
+                        if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
+                    } else {
+                        finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, n, cp, row,
+                                    out_ids, out_status, out_probs);
+                    }
+                    if (lane == 0) row_arrivals[row] = 0;  // ready for the next call
                 }
             }
             __syncwarp();
@@ -673,7 +844,8 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         }
         if (lane == 0) {
             // Rows this warp could not finish because a wait gave up.
-            for (; row < rows; row += gridDim.x) {
+            for (; u < units; u += gridDim.x) {
+                const size_t row = u / splits;
                 if (kRecord) {
                     reinterpret_cast<ShardRecordHeader *>(records + row * rec_bytes)->flags = 2;
                 } else {
@@ -690,7 +862,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
     const float scale = cp.scale;
     const uint32_t t_bound = cp.topk_active ? (cp.top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
     uint32_t consumed = 0, par = 0, j = 0;
-    for (size_t row = blockIdx.x; row < rows; row += gridDim.x, ++j) {
+    for (size_t u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+        const size_t row = u / splits;
+        const uint32_t seg = static_cast<uint32_t>(u % splits);
         const uint32_t b = j & 1u;
         bool bad = false;
         if (threadIdx.x == 0) {
@@ -703,6 +877,8 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         uint32_t *count = &sm.count[b];
         uint32_t *ovf = &sm.overflow[b];
         const RowGeom g = row_geom(logits, row, row_stride, vocab);
+        const uint32_t c0 = seg_begin(g.nchunks, seg, splits);
+        const uint32_t c1 = seg_begin(g.nchunks, seg + 1, splits);
         // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
         // NaN (NaN reads as -inf in the reference, and -inf never survives);
         // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
@@ -728,8 +904,8 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             const uint32_t ntail = vocab - g.head - g.nbody;
             const uint32_t i = threadIdx.x;
             uint32_t idx = ~0u;
-            if (i < g.head) idx = i;
-            else if (i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
+            if (seg == 0 && i < g.head) idx = i;
+            else if (seg == splits - 1 && i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
             float v = kNegInf;
             if (idx != ~0u) {
                 v = __fmul_rn(g.p[idx], scale);
@@ -740,13 +916,13 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         }
         bool stop = false;
         bool got = true, mark = false;
-        for (uint32_t c = 0; c < g.nchunks; ++c) {
+        for (uint32_t c = c0; c < c1; ++c) {
             const uint32_t s = consumed % kStages;
             got &= mbar_wait(&sm.full[s], (consumed / kStages) & 1u);
             const uint32_t len = min(kChunk, g.nbody - c * kChunk);
             const float4 *r4 = reinterpret_cast<const float4 *>(sm.ring[s]);
             const uint32_t base_idx = g.head + c * kChunk + index_offset;
-            if (c == 0 && t_bound) {
+            if (c == c0 && t_bound) {
                 // First chunk: lane maxima before filtering, so that tau is
                 // already high for this chunk's own logits.
                 float cmr = kNegInf;
@@ -804,9 +980,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 }
                 if (m) mark |= append_mask(L, count, ovf, m, v, base_idx + 4 * threadIdx.x, kCompactAt);
             }
-            const bool last = c + 1 == g.nchunks;
+            const bool last = c + 1 == c1;
             // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
-            const uint32_t done = c + 1;
+            const uint32_t done = c + 1 - c0;
             const bool refresh = last || (done < 8 ? (done & (done - 1)) == 0 && done > 1 : done % 8 == 0);
             if (!refresh) continue;
             if (t_bound) post_warp_bound(sm, lmax, t_bound, cw, par);
@@ -899,44 +1075,13 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     CandList &L = sm.list[warp];
     FinishWork &fw = sm.fw[warp];
-    const uint32_t cap_entries = cp.top_k + RSC_SHARD_TIE_CAP;
     for (size_t row = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; row < rows;
          row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
-        uint32_t count = 0;
-        bool bad = false;
-        for (size_t s = 0; s < n_shards; ++s) {
-            const unsigned char *rec = records + (s * rows + row) * rec_bytes;
-            const ShardRecordHeader *h = reinterpret_cast<const ShardRecordHeader *>(rec);
-            const uint32_t *rkey = reinterpret_cast<const uint32_t *>(rec + sizeof(ShardRecordHeader));
-            const uint32_t *ridx = rkey + cap_entries;
-            const uint32_t nc = h->flags ? 0u : min(h->n_cand, cap_entries);
-            if (h->flags || count + nc > kCap) bad = true;
-            for (uint32_t i = lane; i < nc; i += 32) {
-                if (count + i < kCap) {
-                    L.key[count + i] = rkey[i];
-                    L.idx[count + i] = ridx[i];
-                }
-            }
-            count += nc;
-        }
-        __syncwarp();
-        if (!bad) {
-            // A shard that dropped tied entries is harmless only if everything
-            // it dropped lies below the global threshold.
-            uint32_t floor_key = 0u;
-            const bool have_kth = cp.topk_active && count >= cp.top_k;
-            if (have_kth) {
-                const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
-                    count, cp.top_k, [&](uint32_t i) { return L.key[i]; }, fw.hist, fw.sel);
-                floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
-            }
-            for (size_t s = 0; s < n_shards; ++s) {
-                const ShardRecordHeader *h =
-                    reinterpret_cast<const ShardRecordHeader *>(records + (s * rows + row) * rec_bytes);
-                if (h->n_dropped > 0 && (!have_kth || h->last_key >= floor_key)) bad = true;
-            }
-        }
-        if (bad) {
+        bool ok = true;
+        const uint32_t count = merge_records(
+            L, fw, [&](uint32_t part) { return records + (part * rows + row) * rec_bytes; },
+            static_cast<uint32_t>(n_shards), cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
+        if (!ok) {
             if (lane == 0) {
                 out_ids[row] = 0;
                 out_status[row] = RSC_ROW_INTERNAL;
@@ -961,18 +1106,47 @@ cudaError_t prepare(K kernel, size_t smem) {
 
 size_t stream_topk_smem_bytes() { return sizeof(StreamSmem); }
 
+size_t split_record_bytes(uint32_t splits) {
+    const size_t entries = kSmallCap / (splits ? splits : 1u);
+    return (sizeof(ShardRecordHeader) + 8 * entries + 15) & ~static_cast<size_t>(15);
+}
+
+uint32_t stream_splits(size_t rows, uint32_t vocab, uint32_t top_k, int num_sms,
+                       size_t max_units) {
+    // A segment costs a record, a merge and a finisher pass of its own, which
+    // measured more than the balance it buys once every CTA has a row of its
+    // own. Batches that leave at least half the CTAs idle are split, so that
+    // a few rows still stream over many SMs.
+    const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
+    if (rows == 0 || rows * 2 > ctas) return 1u;
+    const uint32_t nchunks = ((vocab / 4u) * 4u + kChunk - 1) / kChunk;
+    // The merged records (at most kCap / splits entries each) must fit one
+    // candidate list and still hold k plus ties.
+    uint32_t max_splits = kCap / (top_k + RSC_SHARD_TIE_CAP);
+    if (max_splits > kMaxSplits) max_splits = kMaxSplits;
+    if (max_splits > nchunks) max_splits = nchunks;
+    uint32_t s = static_cast<uint32_t>(ctas / rows);
+    if (s > max_splits) s = max_splits;
+    while (s > 1 && rows * s > max_units) --s;
+    return s < 1 ? 1u : s;
+}
+
 cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                size_t row_stride, const CallParams &p, uint32_t *out_ids,
                                int32_t *out_status, float *out_probs, uint32_t *large_rows,
-                               uint32_t *large_count, int num_sms, cudaStream_t stream) {
+                               uint32_t *large_count, uint32_t splits, void *seg_records,
+                               uint32_t *row_arrivals, int num_sms, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
     cudaError_t e = prepare(stream_topk_kernel<false>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
+    if (splits < 1 || !p.topk_active) splits = 1;
     const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
-    const size_t grid = rows < ctas ? rows : ctas;
+    const size_t units = rows * splits;
+    const size_t grid = units < ctas ? units : ctas;
     stream_topk_kernel<false><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
-        large_count, 0u, nullptr, 0);
+        large_count, 0u, nullptr, split_record_bytes(splits), splits,
+        static_cast<unsigned char *>(seg_records), row_arrivals);
     return cudaGetLastError();
 }
 
@@ -987,7 +1161,7 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
     const size_t grid = rows < ctas ? rows : ctas;
     stream_topk_kernel<true><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, nullptr,
-        shard_offset, static_cast<unsigned char *>(records), rec_bytes);
+        shard_offset, static_cast<unsigned char *>(records), rec_bytes, 1u, nullptr, nullptr);
     return cudaGetLastError();
 }
 
