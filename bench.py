@@ -8,6 +8,11 @@ top-p 0.95, per-row uniforms). For N > 1 (torchrun, one rank per GPU) every
 rank samples its own batch of the same shape (weak scaling, rows sharded with
 no collective); the time is the max over ranks. Rank 0 prints one JSON line.
 
+--config cfg4 with N > 1 runs the vocab-sharded mode instead: every rank holds
+1/N of the columns of all 8192 rows, builds its shard records
+(rsc_shard_partial), all-gathers them with NCCL over NVLink, and merges
+(rsc_shard_merge); the job's rows are fixed (strong scaling).
+
 `--impl reference` times the reference's CPU path instead: the C++
 restatement of rusticide-sampling (oracle/, the reference's Rust cannot be
 built on this image) on all host cores, on bounded samples of the same
@@ -65,9 +70,10 @@ def committed_traffic(config: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clock and throttle-reason samples while the benchmark runs."""
+    """nvidia-smi clock and throttle-reason samples while the benchmark runs;
+    `stop(window)` keeps the samples taken inside the timed region."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -85,7 +91,17 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
-    def stop(self) -> dict:
+    @staticmethod
+    def _when(stamp: str):
+        from datetime import datetime
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
+            try:
+                return datetime.strptime(stamp, fmt).timestamp()
+            except ValueError:
+                pass
+        return None
+
+    def stop(self, window=None) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -97,11 +113,17 @@ class ClockSampler:
         rows = []
         for line in Path(self.tmp.name).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
+            if len(parts) >= 10:
                 rows.append(parts)
         os.unlink(self.tmp.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        scope = "whole run"
+        if window is not None:
+            inside = [r for r in rows
+                      if (w := self._when(r[0])) is not None and window[0] <= w <= window[1]]
+            if inside:
+                rows, scope = inside, "timed region"
 
         def num(s):
             try:
@@ -109,17 +131,19 @@ class ClockSampler:
             except ValueError:
                 return None
 
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        sm = [num(r[2]) for r in rows if num(r[2]) is not None]
+        mx = [num(r[3]) for r in rows if num(r[3]) is not None]
+        pw = [num(r[4]) for r in rows if num(r[4]) is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
         for r in rows:
-            for name, val in zip(names, r[5:9]):
+            for name, val in zip(names, r[6:10]):
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "power_w": statistics.median(pw) if pw else None,
+                "reasons": sorted(reasons), "samples": len(rows), "scope": scope}
 
 
 def device_logits(cfg, rows: int, seed: int, device):
@@ -139,7 +163,7 @@ def device_logits(cfg, rows: int, seed: int, device):
     return x.contiguous(), u
 
 
-def cpu_baseline(x_host, u_host, params, seconds: float, threads: int) -> dict:
+def cpu_baseline(x_host, u_host, params, seconds: float, threads: int, greedy: bool = False) -> dict:
     """The oracle (C++ restatement of the reference) on the host cores, on
     repeated passes over a sample of the rows, for about `seconds`."""
     from oracle import oracle as O
@@ -147,7 +171,10 @@ def cpu_baseline(x_host, u_host, params, seconds: float, threads: int) -> dict:
     rows = 0
     t0 = time.perf_counter()
     while True:
-        O.sample_rows(x_host, op, u_host, threads=threads)
+        if greedy:
+            O.greedy_rows(x_host, threads=threads)
+        else:
+            O.sample_rows(x_host, op, u_host, threads=threads)
         rows += x_host.shape[0]
         if time.perf_counter() - t0 >= seconds:
             break
@@ -169,11 +196,28 @@ def run_reference(args, cfg, rank: int, world: int) -> None:
     u = synth.uniforms(sample_rows, seed=99)
     params = SamplingParams(cfg.temperature, cfg.top_k, cfg.top_p)
     op = O.params(cfg.temperature, cfg.top_k, cfg.top_p)
+
+    def ref_step():
+        if cfg.greedy:
+            O.greedy_rows(x, threads=threads)
+        else:
+            O.sample_rows(x, op, u, threads=threads)
+
+    # Bound the whole run to about `ref_seconds`: shrink the per-step sample
+    # (down to one row per thread) when K steps of the first size would not fit.
+    t_w = time.perf_counter()
+    ref_step()
+    per_step = time.perf_counter() - t_w
+    budget = args.ref_seconds / max(args.steps + args.warmup, 1)
+    if per_step > budget:
+        sample_rows = max(threads, int(sample_rows * budget / per_step))
+        sample_rows = min(sample_rows, x.shape[0])
+        x, u = np.ascontiguousarray(x[:sample_rows]), np.ascontiguousarray(u[:sample_rows])
     for _ in range(args.warmup):
-        O.sample_rows(x, op, u, threads=threads)
+        ref_step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        O.sample_rows(x, op, u, threads=threads)
+        ref_step()
     dt = time.perf_counter() - t0
     value = sample_rows * args.steps / dt
     line = {
@@ -204,12 +248,14 @@ def run_reference(args, cfg, rank: int, world: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="cfg2p")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=150.0,
+                    help="bound on the reference arm's run time")
     ap.add_argument("--rows", type=int, default=0,
                     help="rows per GPU (default: the config's); for small profiling captures")
     args = ap.parse_args()
@@ -231,6 +277,7 @@ def main() -> None:
     from datetime import timedelta
 
     from rusticide_b200 import SamplingParams, engine
+    from rusticide_b200.sharding import VocabShardedSampler
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -244,14 +291,30 @@ def main() -> None:
 
     params = SamplingParams(cfg.temperature, cfg.top_k, cfg.top_p)
     rows, vocab = (args.rows or cfg.rows), cfg.vocab
-    x, u = device_logits(cfg, rows, 1234 + 7919 * rank, device)
+    sharded = cfg.name == "cfg4" and world > 1
     eng = engine(local)
-    eng.ensure(rows, vocab)
+    if sharded:
+        # This rank's columns of every row (spikes spread over the shards),
+        # and the same per-row uniforms on every rank: the merge must draw
+        # identically everywhere.
+        vs = VocabShardedSampler(eng, vocab)
+        spk = max(1, cfg.spikes[0] // world)
+        x, _ = device_logits(synth.Config(cfg.name, rows, vs.width, cfg.temperature, cfg.top_k,
+                                          cfg.top_p, cfg.dist, (spk, spk)),
+                             rows, 1234 + 7919 * rank, device)
+        g = torch.Generator(device=device).manual_seed(4321)
+        u = torch.rand(rows, device=device, generator=g)
+        eng.ensure(rows, vs.width)
+    else:
+        x, u = device_logits(cfg, rows, 1234 + 7919 * rank, device)
+        eng.ensure(rows, vocab)
     outs = eng._outputs(rows, True)
     stream = torch.cuda.current_stream(device)
 
     def step():
-        if cfg.greedy:
+        if sharded:
+            vs.sample(x, params, uniforms=u, out=outs)
+        elif cfg.greedy:
             eng.greedy(x, out=outs)
         else:
             eng.sample(x, params, uniforms=u, out=outs)
@@ -268,11 +331,13 @@ def main() -> None:
     launches0 = eng.launch_count()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     ev0.record(stream)
     for _ in range(args.steps):
         step()
     ev1.record(stream)
     torch.cuda.synchronize(device)
+    wall1 = time.time()
     barrier()
     torch.cuda.synchronize(device)
     launches = eng.launch_count() - launches0
@@ -288,23 +353,44 @@ def main() -> None:
         b.record(stream)
         per.append((a, b))
     torch.cuda.synchronize(device)
-    clk = clocks.stop()
+    clk = clocks.stop((wall0, wall1))
     call_ms = statistics.mean(a.elapsed_time(b) for a, b in per)
 
     # End to end through the host-buffer entry point: H2D of the logits and
     # uniforms, sampling, D2H of ids, statuses and probabilities, every step.
-    x_host = torch.empty((rows, vocab), dtype=torch.float32, pin_memory=True)
-    x_host.copy_(x)
-    u_host = torch.empty(rows, dtype=torch.float32, pin_memory=True)
-    u_host.copy_(u)
-    xh, uh = x_host.numpy(), u_host.numpy()
-    eng.pick_host(xh, params, None if cfg.greedy else uh)  # warm
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        eng.pick_host(xh, params, None if cfg.greedy else uh)
-    e2e_s = time.perf_counter() - t0
-    barrier()
+    e2e_rows = rows
+    if sharded:
+        # The host-buffer entry point samples whole rows; the sharded job's
+        # end-to-end figure is the device-resident step plus the copies of
+        # this rank's shard in and the results out.
+        x_host = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
+        x_host.copy_(x)
+        res_host = torch.empty(rows * 3, dtype=torch.int32, pin_memory=True)
+        torch.cuda.synchronize(device)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            step()
+            res_host[:rows].copy_(outs[0], non_blocking=True)
+            res_host[rows:2 * rows].copy_(outs[1], non_blocking=True)
+            res_host[2 * rows:].copy_(outs[2].view(torch.int32), non_blocking=True)
+            torch.cuda.synchronize(device)
+        e2e_s = time.perf_counter() - t0
+        barrier()
+    else:
+        x_host = torch.empty((rows, vocab), dtype=torch.float32, pin_memory=True)
+        x_host.copy_(x)
+        u_host = torch.empty(rows, dtype=torch.float32, pin_memory=True)
+        u_host.copy_(u)
+        xh, uh = x_host.numpy(), u_host.numpy()
+        eng.pick_host(xh, params, None if cfg.greedy else uh)  # warm
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            eng.pick_host(xh, params, None if cfg.greedy else uh)
+        e2e_s = time.perf_counter() - t0
+        barrier()
 
     t_max = t_ms
     e2e_max = e2e_s
@@ -316,18 +402,23 @@ def main() -> None:
     cpu = None
     if rank == 0 and world == 1:
         n_cpu = min(rows, 256)
-        cpu = cpu_baseline(x[:n_cpu].cpu().numpy(), u[:n_cpu].cpu().numpy(), params,
-                           args.cpu_seconds, os.cpu_count() or 1)
+        if cfg.greedy:
+            params_cpu = SamplingParams(0.0, cfg.top_k, cfg.top_p)
+        else:
+            params_cpu = params
+        cpu = cpu_baseline(x[:n_cpu].cpu().numpy(), u[:n_cpu].cpu().numpy(), params_cpu,
+                           args.cpu_seconds, os.cpu_count() or 1, cfg.greedy)
 
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
 
-    total_rows = rows * world * args.steps
+    job_rows = rows if sharded else rows * world
+    total_rows = job_rows * args.steps
     value = total_rows / (t_max / 1000.0)
     peak, peak_kind = measured_peak()
-    alg_bytes = rows * vocab * 4
+    alg_bytes = rows * (x.shape[1] if sharded else vocab) * 4
     achieved = alg_bytes / (call_ms / 1000.0) / 1e9
     traffic = committed_traffic(args.config)
     line = {
@@ -339,22 +430,24 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": t_max / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if sharded else "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": cfg.name, "rows_per_gpu": rows, "vocab": vocab,
                    "temperature": cfg.temperature, "top_k": cfg.top_k, "top_p": cfg.top_p,
                    "mode": "greedy" if cfg.greedy else "sample_logits",
-                   "parallelism": f"row-sharded x{world}",
+                   "parallelism": (f"vocab-sharded x{world} (NCCL all-gather of shard records)"
+                                   if sharded else f"row-sharded x{world}"),
                    "l2": f"inputs {alg_bytes / 2**20:.0f} MiB > 126 MiB L2 (no flush needed)"},
         "hbm_gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "note": "achieved = rows*vocab*4 B / mean CUDA-event time of one rsc_sample call"},
-        "e2e": {"value": rows * world * args.e2e_steps / e2e_max, "unit": "rows/s",
-                "h2d_bytes_per_step": rows * vocab * 4 + (0 if cfg.greedy else rows * 4),
+        "e2e": {"value": job_rows * args.e2e_steps / e2e_max, "unit": "rows/s",
+                "h2d_bytes_per_step": (rows * x.shape[1] * 4 if sharded else
+                                       rows * vocab * 4 + (0 if cfg.greedy else rows * 4)),
                 "d2h_bytes_per_step": rows * 12},
         "gpu_launches": launches,
         "clocks": clk,

@@ -1,0 +1,93 @@
+"""Multi-GPU layouts of the sampler: one process per GPU.
+
+Two ways to spread a batch over GPUs:
+
+* row-sharded (`row_shard`): every rank samples whole rows of its own slice of
+  the batch; rows are independent, so there is no collective on the data path
+  (weak scaling).
+* vocab-sharded (`VocabShardedSampler`): every rank holds the same rows but
+  only a contiguous slice of the vocabulary, as a tensor-parallel LM head
+  leaves them. Each rank reduces its slice to a fixed-size shard record per
+  row (rsc_shard_partial: the slice's top-(k + tie slack) candidates in the
+  total order), the records are all-gathered (NCCL over NVLink on B200), and
+  every rank merges the gathered records into the same token per row
+  (rsc_shard_merge). Only records cross NVLink: rows x ranks x
+  rsc_shard_record_bytes(k) bytes (544 B per row and rank at k = 40)
+  instead of the slices of the logits.
+
+The reference samples whole rows on one host (crates/rusticide-sampling/src/
+sampler.rs:44 sample_logits, :75 greedy_logits); sharding is this
+implementation's own layer on top of the same per-row result, so a sharded
+batch must give the tokens of the unsharded call bit for bit.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def vocab_shard(vocab: int, world: int, rank: int) -> Tuple[int, int]:
+    """(offset, width) of rank's vocabulary slice: equal slices of
+    vocab // world columns, the last rank taking the remainder."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    if vocab < world:
+        raise ValueError(f"vocab {vocab} smaller than world {world}")
+    base = vocab // world
+    offset = rank * base
+    width = vocab - offset if rank == world - 1 else base
+    return offset, width
+
+
+def row_shard(rows: int, world: int, rank: int) -> Tuple[int, int]:
+    """(start, count) of rank's rows: the first rows % world ranks take one
+    row more than the others, so counts differ by at most one."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    base, extra = divmod(rows, world)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+class VocabShardedSampler:
+    """partial -> all-gather -> merge over a process group.
+
+    `engine` is a rusticide_b200.Engine (or any object with its
+    shard_record_bytes / shard_partial / shard_merge methods). Every rank
+    must call `sample` with the same rows, params and uniforms; the result
+    (ids, status, probs) is the same on every rank.
+    """
+
+    def __init__(self, engine, vocab: int, group: Optional[dist.ProcessGroup] = None):
+        self.engine = engine
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.vocab = int(vocab)
+        self.offset, self.width = vocab_shard(self.vocab, self.world, self.rank)
+        self._bufs: dict = {}
+
+    def _buffers(self, rows: int, top_k: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+        key = (rows, top_k, str(device))
+        if key not in self._bufs:
+            rb = self.engine.shard_record_bytes(top_k)
+            records = torch.empty(rows * rb, dtype=torch.uint8, device=device)
+            gathered = torch.empty(self.world * rows * rb, dtype=torch.uint8, device=device)
+            self._bufs = {key: (records, gathered)}
+        return self._bufs[key]
+
+    def sample(self, logits_shard: torch.Tensor, params, uniforms: Optional[torch.Tensor] = None,
+               rng_states: Optional[torch.Tensor] = None, want_probs: bool = True, out=None):
+        if logits_shard.dim() != 2 or logits_shard.shape[1] != self.width:
+            raise ValueError(f"rank {self.rank} expects [rows, {self.width}] logits, "
+                             f"got {tuple(logits_shard.shape)}")
+        rows = logits_shard.shape[0]
+        records, gathered = self._buffers(rows, params.top_k, logits_shard.device)
+        self.engine.shard_partial(logits_shard, self.offset, self.vocab, params, records=records)
+        dist.all_gather_into_tensor(gathered, records, group=self.group)
+        return self.engine.shard_merge(gathered, self.world, rows, self.vocab, params,
+                                       uniforms=uniforms, rng_states=rng_states,
+                                       want_probs=want_probs, out=out)

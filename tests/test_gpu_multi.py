@@ -1,0 +1,94 @@
+"""Vocab-sharded sampling across GPUs: NCCL ranks, one process per GPU.
+
+Each rank holds one vocabulary slice of the same rows; partial records are
+all-gathered over NVLink and merged (rusticide_b200.sharding). Every rank must
+return the tokens, statuses and probabilities that the unsharded single-GPU
+call returns on the whole rows (bit for bit), and those match the oracle.
+Skipped unless at least two GPUs are visible.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from rusticide_b200 import SamplingParams, synth
+
+pytestmark = pytest.mark.gpu
+
+ROWS, VOCAB = 64, 151936
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    from rusticide_b200 import engine
+    from rusticide_b200.sharding import VocabShardedSampler
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        x = synth.make_logits(ROWS, VOCAB, base_seed=31)
+        u = synth.uniforms(ROWS, seed=8)
+        params = SamplingParams(0.8, 40, 0.95)
+        vs = VocabShardedSampler(engine(rank), VOCAB)
+        mine = torch.from_numpy(np.ascontiguousarray(x[:, vs.offset:vs.offset + vs.width])).to(dev)
+        ids, status, probs = vs.sample(mine, params, uniforms=torch.from_numpy(u).to(dev))
+        torch.cuda.synchronize(dev)
+        q.put((rank, ids.cpu().numpy().tolist(), status.cpu().numpy().tolist(),
+               probs.cpu().numpy().view(np.uint32).tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_vocab_sharded_nccl_matches_unsharded():
+    from oracle import oracle as O
+    from rusticide_b200 import engine
+    world = min(torch.cuda.device_count(), 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    while len(got) < world:
+        try:
+            rank, ids, st, pb = q.get(timeout=5)
+            got[rank] = (ids, st, pb)
+        except Exception:
+            if not all(p.is_alive() or p.exitcode == 0 for p in procs):
+                for p in procs:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("a rank failed")
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+
+    x = synth.make_logits(ROWS, VOCAB, base_seed=31)
+    u = synth.uniforms(ROWS, seed=8)
+    params = SamplingParams(0.8, 40, 0.95)
+    dev = torch.device("cuda", 0)
+    ids, st, pb = engine(0).sample(torch.from_numpy(x).to(dev), params,
+                                   uniforms=torch.from_numpy(u).to(dev))
+    want = (ids.cpu().numpy().tolist(), st.cpu().numpy().tolist(),
+            pb.cpu().numpy().view(np.uint32).tolist())
+    for r in range(world):
+        assert got[r] == want, f"rank {r}"
+    ref = O.sample_rows(x, O.params(0.8, 40, 0.95), u, threads=4)
+    assert want[0] == [int(t) for t in ref["token"]]
