@@ -24,6 +24,10 @@ struct rsc_sampler {
     uint32_t *large_count = nullptr;  // [2]: list length, drain exit count
     uint32_t *scratch = nullptr;      // [large_slots][4 * max_vocab]
     size_t max_units = 0;             // row segments of the streaming kernel
+    rsc::StreamPlan plan{};           // schedule of the last streaming call
+    size_t plan_rows = 0;
+    uint32_t plan_vocab = 0, plan_topk = 0;
+    bool plan_valid = false;
     void *seg_records = nullptr;      // [max_units] records of split_record_bytes(splits >= 2)
     uint32_t *row_arrivals = nullptr; // [max_rows], zero between calls
     // Device staging of rsc_pick_host.
@@ -103,10 +107,18 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
     cudaError_t e;
     if (small) {
         // large_count is zero here: the draining kernel resets it.
-        const uint32_t splits = rsc::stream_splits(rows, v, cp.top_k, s->num_sms, s->max_units);
+        if (!s->plan_valid || s->plan_rows != rows || s->plan_vocab != v ||
+            s->plan_topk != (cp.topk_active ? cp.top_k : 0u)) {
+            s->plan = rsc::stream_plan(rows, v, cp.topk_active, cp.top_k, s->num_sms,
+                                       s->max_units * rsc::split_record_bytes(2));
+            s->plan_rows = rows;
+            s->plan_vocab = v;
+            s->plan_topk = cp.topk_active ? cp.top_k : 0u;
+            s->plan_valid = true;
+        }
         e = rsc::launch_stream_topk(logits, rows, v, row_stride, cp, ids, status, probs,
-                                    s->large_rows, s->large_count, splits, s->seg_records,
-                                    s->row_arrivals, s->num_sms, stream);
+                                    s->large_rows, s->large_count, s->plan, s->seg_records,
+                                    s->row_arrivals, stream);
         ++s->launches;
         if (e != cudaSuccess) return RSC_ERR_CUDA;
         e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->large_rows,

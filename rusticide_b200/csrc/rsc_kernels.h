@@ -20,30 +20,39 @@ cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size
                           uint32_t *out_ids, int32_t *out_status, int num_sms,
                           cudaStream_t stream);
 
-// Most segments a row is cut into by the streaming kernel.
+// Most CTAs a row is spread over by the streaming kernel.
 constexpr uint32_t kStreamMaxSplits = 16;
 
-// Bytes of one segment record when rows are split `splits` ways (kSmallCap /
-// splits entries).
-size_t split_record_bytes(uint32_t splits);
+// Bytes of one part record when a row is spread over `parts` CTAs (kSmallCap /
+// parts entries).
+size_t split_record_bytes(uint32_t parts);
 
-// Number of segments per row that spreads `rows` best over the streaming
-// kernel's CTAs (rows * result <= max_units, and the segments' merged
-// records fit one candidate list).
-uint32_t stream_splits(size_t rows, uint32_t vocab, uint32_t top_k, int num_sms,
-                       size_t max_units);
+// Work schedule of the streaming kernel: its grid, the chunks per row, and
+// whether CTAs take balanced chunk ranges (rows spread over up to max_parts
+// CTAs) or whole rows round-robin.
+struct StreamPlan {
+    uint32_t grid;
+    uint32_t nch;
+    uint32_t streamk;
+    uint32_t max_parts;
+};
+
+// The schedule for a call; seg_capacity_bytes is the size of the handle's
+// part-record buffer (rows * max_parts * split_record_bytes(max_parts) must
+// fit, else whole rows are used).
+StreamPlan stream_plan(size_t rows, uint32_t vocab, bool topk_active, uint32_t top_k,
+                       int num_sms, size_t seg_capacity_bytes);
 
 // Streaming top-k kernel for rows whose survivors fit kSmallCap. Rows that
-// overflow are appended to large_rows[large_count[0]]. With splits > 1 each
-// row is cut into that many segments; seg_records (rows * splits records of
-// shard_record_bytes(top_k)) and row_arrivals (rows counters, zero on entry
-// and on exit) carry the segments' candidates to the segment that finishes
-// the row.
+// overflow are appended to large_rows[large_count[0]]. A row spread over
+// several CTAs leaves one record per part in seg_records (rows * max_parts
+// records of split_record_bytes(max_parts)); row_arrivals (rows counters,
+// zero on entry and on exit) tells the last part to merge them.
 cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                size_t row_stride, const CallParams &p, uint32_t *out_ids,
                                int32_t *out_status, float *out_probs, uint32_t *large_rows,
-                               uint32_t *large_count, uint32_t splits, void *seg_records,
-                               uint32_t *row_arrivals, int num_sms, cudaStream_t stream);
+                               uint32_t *large_count, const StreamPlan &plan, void *seg_records,
+                               uint32_t *row_arrivals, cudaStream_t stream);
 
 // Large-survivor kernel. With large_rows == nullptr it processes rows
 // [0, rows); otherwise the rows listed in large_rows[0 .. large_count[0]),
@@ -60,9 +69,9 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
 // and uint32 index[k + RSC_SHARD_TIE_CAP] (global indices), entries sorted by
 // (key desc, index asc). Keys are f32::total_cmp keys of the scaled logits.
 struct ShardRecordHeader {
-    float max_scaled;    // max of the shard's scaled logits (f32::max fold)
-    float sum_exp;       // sum of exp(v - max_scaled) over the shard (fast exp; diagnostic)
-    uint32_t n_finite;   // logits that are not -inf
+    float max_scaled;    // max of the shard's scaled logits, NaN skipped (diagnostic)
+    float sum_exp;       // reserved, 0
+    uint32_t n_finite;   // reserved, 0
     uint32_t n_cand;     // entries that follow
     uint32_t n_dropped;  // entries at or above the local threshold that did not fit
     uint32_t last_key;   // key of the last entry

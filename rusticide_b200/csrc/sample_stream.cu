@@ -85,8 +85,6 @@ struct StreamSmem {
     float tau_final[2];  // the consumers' last bound of the row (<= its k-th largest value)
     float warp_tau[2][kConsumerWarps];
     float st_max[2][kConsumerWarps];
-    float st_sum[2][kConsumerWarps];
-    uint32_t st_cnt[2][kConsumerWarps];
     uint32_t chist[256];
     uint32_t csel[2];
     uint32_t error;
@@ -132,10 +130,9 @@ __device__ __forceinline__ bool consumers_any(bool p) {
     return r != 0;
 }
 
-// Appends the logits of this thread's chunk slice whose bit is set in `m`
-// (bit 4*jj + e: element e of float4 jj, global index i0 + 4*kConsumers*jj + e).
-// One shared atomic per thread that has any. Returns true if the list grew
-// past `mark`.
+// Appends the logits whose bit is set in `m` (bit 4*jj + e: element e of
+// float4 jj, global index i0 + 4*kConsumers*jj + e) with one shared atomic.
+// Returns true if the list grew past `mark`.
 template <int N>
 __device__ __forceinline__ bool append_mask(CandList &L, uint32_t *count, uint32_t *overflow,
                                             uint32_t m, const float (&v)[N], uint32_t i0,
@@ -682,9 +679,59 @@ __device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uin
     return min(count, kCap);
 }
 
-// First chunk of segment `seg` of a row of `nchunks` chunks split `splits` ways.
-__device__ __forceinline__ uint32_t seg_begin(uint32_t nchunks, uint32_t seg, uint32_t splits) {
-    return static_cast<uint32_t>((static_cast<unsigned long long>(nchunks) * seg) / splits);
+// --- work schedule -------------------------------------------------------------
+//
+// The batch is rows x nch chunks (nch = ceil(vocab / kChunk), the same for
+// every row; chunks past a row's own body are empty). Two schedules:
+//  - whole rows, round-robin over the CTAs (streamk = 0);
+//  - balanced ranges (streamk = 1): CTA b takes the chunks
+//    [b*T/G, (b+1)*T/G) of the batch in row-major order, T = rows * nch,
+//    G = gridDim.x. A row whose chunks fall to several CTAs is finished by
+//    the last of its parts to arrive, from the parts' records. Every CTA
+//    streams the same number of chunks (+-1), so no SM idles while another
+//    finishes a last row.
+struct Piece {
+    size_t row;
+    uint32_t c0, c1;  // chunks [c0, c1) of the row
+    uint32_t part;    // this CTA's part of the row, 0 .. nparts-1
+    uint32_t nparts;
+};
+
+// The CTA that owns global chunk x under the balanced schedule: the largest
+// b with floor(b*T/G) <= x.
+__device__ __forceinline__ uint32_t chunk_owner(unsigned long long x, unsigned long long T,
+                                                uint32_t G) {
+    return static_cast<uint32_t>(((x + 1ull) * G - 1ull) / T);
+}
+
+// The u-th piece of this CTA; false past the last.
+__device__ __forceinline__ bool get_piece(size_t rows, uint32_t nch, uint32_t streamk, uint32_t u,
+                                          Piece &pc) {
+    if (!streamk) {
+        const size_t row = blockIdx.x + static_cast<size_t>(u) * gridDim.x;
+        if (row >= rows) return false;
+        pc.row = row;
+        pc.c0 = 0;
+        pc.c1 = nch;
+        pc.part = 0;
+        pc.nparts = 1;
+        return true;
+    }
+    const unsigned long long T = static_cast<unsigned long long>(rows) * nch;
+    const unsigned long long G = gridDim.x;
+    const unsigned long long begin = T * blockIdx.x / G;
+    const unsigned long long end = T * (blockIdx.x + 1ull) / G;
+    const size_t row = static_cast<size_t>(begin / nch) + u;
+    const unsigned long long rs = static_cast<unsigned long long>(row) * nch;
+    if (rs >= end) return false;
+    pc.row = row;
+    pc.c0 = static_cast<uint32_t>((begin > rs ? begin : rs) - rs);
+    pc.c1 = static_cast<uint32_t>((end < rs + nch ? end : rs + nch) - rs);
+    const uint32_t first = chunk_owner(rs, T, gridDim.x);
+    const uint32_t last = chunk_owner(rs + nch - 1ull, T, gridDim.x);
+    pc.part = blockIdx.x - first;
+    pc.nparts = last - first + 1u;
+    return true;
 }
 
 // --- the streaming kernel -------------------------------------------------------
@@ -696,16 +743,16 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs,
                    uint32_t *__restrict__ large_rows, uint32_t *__restrict__ large_count,
                    uint32_t index_offset, unsigned char *__restrict__ records, size_t rec_bytes,
-                   uint32_t splits, unsigned char *__restrict__ seg_records,
-                   uint32_t *__restrict__ row_arrivals) {
+                   uint32_t nch, uint32_t streamk, uint32_t max_parts,
+                   unsigned char *__restrict__ seg_records, uint32_t *__restrict__ row_arrivals) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     StreamSmem &sm = *reinterpret_cast<StreamSmem *>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // Work units: row r, segment g (unit r * splits + g); a segment is a run
-    // of whole chunks, segment 0 also takes the scalar head, the last segment
-    // the scalar tail.
-    const size_t units = rows * splits;
-    const uint32_t seg_cap = kCap / splits;  // entries of a segment record
+    // Pieces of rows (get_piece): a piece is a run of whole chunks of one row;
+    // the piece that starts at chunk 0 also takes the row's scalar head, the
+    // one that ends at chunk nch the scalar tail. A row cut into several
+    // pieces keeps one record per part (kCap / max_parts entries each).
+    const uint32_t seg_cap = kCap / max_parts;
 
     load_exp_table(sm.exp_tab);
     if (threadIdx.x == 0) {
@@ -730,12 +777,11 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         if (lane != 0) return;
         uint32_t q = 0;
         bool ok = true;
-        for (size_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
-            const size_t row = u / splits;
-            const uint32_t seg = static_cast<uint32_t>(u % splits);
-            const RowGeom g = row_geom(logits, row, row_stride, vocab);
-            const uint32_t c1 = seg_begin(g.nchunks, seg + 1, splits);
-            for (uint32_t c = seg_begin(g.nchunks, seg, splits); c < c1; ++c) {
+        Piece pc;
+        for (uint32_t u = 0; ok && get_piece(rows, nch, streamk, u, pc); ++u) {
+            const RowGeom g = row_geom(logits, pc.row, row_stride, vocab);
+            const uint32_t c1 = min(pc.c1, g.nchunks);
+            for (uint32_t c = pc.c0; c < c1; ++c) {
                 const uint32_t s = q % kStages;
                 if (q >= kStages && !mbar_wait(&sm.empty[s], ((q / kStages) - 1u) & 1u)) {
                     atomicExch(&sm.error, 1u);
@@ -760,11 +806,11 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
     }
 
     if (warp == kFinisherWarp) {
-        uint32_t j = 0;
-        size_t u = blockIdx.x;
-        for (; u < units; u += gridDim.x, ++j) {
-            const size_t row = u / splits;
-            const uint32_t seg = static_cast<uint32_t>(u % splits);
+        uint32_t u = 0;
+        Piece pc;
+        for (; get_piece(rows, nch, streamk, u, pc); ++u) {
+            const size_t row = pc.row;
+            const uint32_t j = u;
             const uint32_t b = j & 1u;
             const bool got = mbar_wait(&sm.list_full[b], (j >> 1) & 1u);
             if (__any_sync(0xffffffffu, !got)) {
@@ -785,18 +831,11 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     }
                 } else {
                     float M = kNegInf;
-                    uint32_t nfin = 0;
-                    for (int w = 0; w < kConsumerWarps; ++w) {
-                        M = fmaxf(M, sm.st_max[b][w]);
-                        nfin += sm.st_cnt[b][w];
-                    }
-                    float S = 0.0f;
-                    for (int w = 0; w < kConsumerWarps; ++w)
-                        if (sm.st_sum[b][w] > 0.0f) S += sm.st_sum[b][w] * __expf(sm.st_max[b][w] - M);
-                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, M, S, nfin, rec,
+                    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.st_max[b][w]);
+                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, M, 0.0f, 0u, rec,
                                 cp.top_k + RSC_SHARD_TIE_CAP, sm.tau_final[b]);
                 }
-            } else if (splits == 1) {
+            } else if (pc.nparts == 1) {
                 if (ov) {
                     if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
                 } else {
@@ -804,9 +843,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                                 out_ids, out_status, out_probs);
                 }
             } else {
-                // One segment of a split row: publish its record, and the
-                // segment that completes the row merges all of them.
-                unsigned char *rec = seg_records + (row * splits + seg) * rec_bytes;
+                // One part of a split row: publish its record, and the part
+                // that completes the row merges all of them.
+                unsigned char *rec = seg_records + (row * max_parts + pc.part) * rec_bytes;
                 if (ov) {
                     if (lane == 0) {
                         ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
@@ -823,13 +862,13 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 uint32_t arrived = 0;
                 if (lane == 0) arrived = atomicAdd(&row_arrivals[row], 1u);
                 arrived = __shfl_sync(0xffffffffu, arrived, 0);
-                if (arrived == splits - 1) {
+                if (arrived == pc.nparts - 1) {
                     __threadfence();
                     bool ok = true;
                     const uint32_t n = merge_records(
                         sm.list[b], sm.fw,
-                        [&](uint32_t part) { return seg_records + (row * splits + part) * rec_bytes; },
-                        splits, seg_cap, cp, &ok);
+                        [&](uint32_t part) { return seg_records + (row * max_parts + part) * rec_bytes; },
+                        pc.nparts, seg_cap, cp, &ok);
                     if (!ok) {
                         if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
                     } else {
@@ -842,17 +881,32 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.list_empty[b]);
         }
-        if (lane == 0) {
-            // Rows this warp could not finish because a wait gave up.
-            for (; u < units; u += gridDim.x) {
-                const size_t row = u / splits;
-                if (kRecord) {
-                    reinterpret_cast<ShardRecordHeader *>(records + row * rec_bytes)->flags = 2;
-                } else {
+        // Pieces this warp could not finish because a wait gave up: their
+        // rows report RSC_ROW_INTERNAL. A part of a split row still publishes
+        // a (failed) record and arrives, so that the row is completed.
+        for (; get_piece(rows, nch, streamk, u, pc); ++u) {
+            const size_t row = pc.row;
+            if (kRecord) {
+                if (lane == 0) reinterpret_cast<ShardRecordHeader *>(records + row * rec_bytes)->flags = 2;
+            } else if (pc.nparts == 1) {
+                if (lane == 0) {
                     out_ids[row] = 0;
                     out_status[row] = RSC_ROW_INTERNAL;
                 }
+            } else if (lane == 0) {
+                ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(
+                    seg_records + (row * max_parts + pc.part) * rec_bytes);
+                h->n_cand = 0;
+                h->n_dropped = 0;
+                h->flags = 2;
+                __threadfence();
+                if (atomicAdd(&row_arrivals[row], 1u) == pc.nparts - 1) {
+                    out_ids[row] = 0;
+                    out_status[row] = RSC_ROW_INTERNAL;
+                    row_arrivals[row] = 0;
+                }
             }
+            __syncwarp();
         }
         return;
     }
@@ -861,10 +915,10 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
     const int cw = warp;
     const float scale = cp.scale;
     const uint32_t t_bound = cp.topk_active ? (cp.top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
-    uint32_t consumed = 0, par = 0, j = 0;
-    for (size_t u = blockIdx.x; u < units; u += gridDim.x, ++j) {
-        const size_t row = u / splits;
-        const uint32_t seg = static_cast<uint32_t>(u % splits);
+    uint32_t consumed = 0, par = 0;
+    Piece pc;
+    for (uint32_t j = 0; get_piece(rows, nch, streamk, j, pc); ++j) {
+        const size_t row = pc.row;
         const uint32_t b = j & 1u;
         bool bad = false;
         if (threadIdx.x == 0) {
@@ -877,39 +931,23 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         uint32_t *count = &sm.count[b];
         uint32_t *ovf = &sm.overflow[b];
         const RowGeom g = row_geom(logits, row, row_stride, vocab);
-        const uint32_t c0 = seg_begin(g.nchunks, seg, splits);
-        const uint32_t c1 = seg_begin(g.nchunks, seg + 1, splits);
+        const uint32_t c0 = pc.c0;
+        const uint32_t c1 = min(pc.c1, g.nchunks);
         // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
         // NaN (NaN reads as -inf in the reference, and -inf never survives);
         // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
         float tau = -3.402823466e38f;
-        float lmax = kNegInf;
-        float mx_t = kNegInf, se_t = 0.0f;
-        uint32_t cnt_t = 0;
-        auto stats = [&](float v) {
-            if (kRecord) {
-                if (v != kNegInf && v == v) {
-                    ++cnt_t;
-                    if (v > mx_t) {
-                        se_t = (mx_t == kNegInf ? 0.0f : se_t * __expf(mx_t - v)) + 1.0f;
-                        mx_t = v;
-                    } else {
-                        se_t += __expf(v - mx_t);
-                    }
-                }
-            }
-        };
+        float lmax = kNegInf;  // this lane's largest scaled logit of the piece
         // Scalar head and tail (at most 3 logits each).
         {
             const uint32_t ntail = vocab - g.head - g.nbody;
             const uint32_t i = threadIdx.x;
             uint32_t idx = ~0u;
-            if (seg == 0 && i < g.head) idx = i;
-            else if (seg == splits - 1 && i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
+            if (pc.c0 == 0 && i < g.head) idx = i;
+            else if (pc.c1 == nch && i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
             float v = kNegInf;
             if (idx != ~0u) {
                 v = __fmul_rn(g.p[idx], scale);
-                stats(v);
                 lmax = fmaxf(lmax, v);
             }
             append_candidate(L, count, ovf, v >= tau, total_key(v), idx + index_offset, kCap);
@@ -945,40 +983,45 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             }
             constexpr uint32_t kPerThread = kChunk / 4 / kConsumers;
             float4 f[kPerThread];
+            if (len == kChunk) {  // every chunk but a row's last
 #pragma unroll
-            for (uint32_t jj = 0; jj < kPerThread; ++jj) {
-                const uint32_t q = threadIdx.x + jj * kConsumers;
-                f[jj] = (4 * q < len) ? r4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+                for (uint32_t jj = 0; jj < kPerThread; ++jj) f[jj] = r4[threadIdx.x + jj * kConsumers];
+            } else {
+#pragma unroll
+                for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                    const uint32_t q = threadIdx.x + jj * kConsumers;
+                    f[jj] = (4 * q < len) ? r4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage s released by this warp
             ++consumed;
             // x -> fl(x * scale) is non-decreasing for a finite scale > 0, so
-            // the largest scaled value of this thread's slice is the scaled
-            // largest raw value: one max per logit decides whether the slice
-            // holds a candidate at all (fmaxf skips NaN, which reads as -inf).
-            float cmr = f[0].x;
+            // the largest scaled value of a group of logits is the scaled
+            // largest raw value: one max per logit decides whether this
+            // thread's slice holds a candidate at all, and one max per float4
+            // which of its float4s do (fmaxf skips NaN, which reads as -inf).
+            float m4[kPerThread];
 #pragma unroll
             for (uint32_t jj = 0; jj < kPerThread; ++jj)
-                cmr = fmaxf(fmaxf(cmr, fmaxf(f[jj].x, f[jj].y)), fmaxf(f[jj].z, f[jj].w));
+                m4[jj] = fmaxf(fmaxf(f[jj].x, f[jj].y), fmaxf(f[jj].z, f[jj].w));
+            float cmr = m4[0];
+#pragma unroll
+            for (uint32_t jj = 1; jj < kPerThread; ++jj) cmr = fmaxf(cmr, m4[jj]);
             const float cm = __fmul_rn(cmr, scale);
             lmax = fmaxf(lmax, cm);
-            if (kRecord || cm >= tau) {
-                float v[4 * kPerThread];
-                uint32_t m = 0;
+            if (cm >= tau) {
 #pragma unroll
                 for (uint32_t jj = 0; jj < kPerThread; ++jj) {
-                    v[4 * jj + 0] = __fmul_rn(f[jj].x, scale);
-                    v[4 * jj + 1] = __fmul_rn(f[jj].y, scale);
-                    v[4 * jj + 2] = __fmul_rn(f[jj].z, scale);
-                    v[4 * jj + 3] = __fmul_rn(f[jj].w, scale);
+                    if (__fmul_rn(m4[jj], scale) >= tau) {
+                        const float v[4] = {__fmul_rn(f[jj].x, scale), __fmul_rn(f[jj].y, scale),
+                                            __fmul_rn(f[jj].z, scale), __fmul_rn(f[jj].w, scale)};
+                        const uint32_t m = (v[0] >= tau ? 1u : 0u) | (v[1] >= tau ? 2u : 0u) |
+                                           (v[2] >= tau ? 4u : 0u) | (v[3] >= tau ? 8u : 0u);
+                        mark |= append_mask(L, count, ovf, m, v,
+                                            base_idx + 4 * (threadIdx.x + jj * kConsumers), kCompactAt);
+                    }
                 }
-#pragma unroll
-                for (uint32_t e = 0; e < 4 * kPerThread; ++e) {
-                    stats(v[e]);
-                    m |= (v[e] >= tau ? 1u : 0u) << e;
-                }
-                if (m) mark |= append_mask(L, count, ovf, m, v, base_idx + 4 * threadIdx.x, kCompactAt);
             }
             const bool last = c + 1 == c1;
             // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
@@ -1030,21 +1073,8 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         }
         if (stop) break;
         if (kRecord) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float om = __shfl_xor_sync(0xffffffffu, mx_t, o);
-                const float os = __shfl_xor_sync(0xffffffffu, se_t, o);
-                const float m2 = fmaxf(mx_t, om);
-                se_t = (se_t > 0.0f ? se_t * __expf(mx_t - m2) : 0.0f) +
-                       (os > 0.0f ? os * __expf(om - m2) : 0.0f);
-                mx_t = m2;
-                cnt_t += __shfl_xor_sync(0xffffffffu, cnt_t, o);
-            }
-            if (lane == 0) {
-                sm.st_max[b][cw] = mx_t;
-                sm.st_sum[b][cw] = se_t;
-                sm.st_cnt[b][cw] = cnt_t;
-            }
+            const float wm = warp_max(lmax);
+            if (lane == 0) sm.st_max[b][cw] = wm;
         }
         if (threadIdx.x == 0) sm.tau_final[b] = tau;
         ConsumerSync::sync();  // the row's list is complete
@@ -1111,42 +1141,76 @@ size_t split_record_bytes(uint32_t splits) {
     return (sizeof(ShardRecordHeader) + 8 * entries + 15) & ~static_cast<size_t>(15);
 }
 
-uint32_t stream_splits(size_t rows, uint32_t vocab, uint32_t top_k, int num_sms,
-                       size_t max_units) {
-    // A segment costs a record, a merge and a finisher pass of its own, which
-    // measured more than the balance it buys once every CTA has a row of its
-    // own. Batches that leave at least half the CTAs idle are split, so that
-    // a few rows still stream over many SMs.
+StreamPlan stream_plan(size_t rows, uint32_t vocab, bool topk_active, uint32_t top_k,
+                       int num_sms, size_t seg_capacity_bytes) {
     const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
-    if (rows == 0 || rows * 2 > ctas) return 1u;
-    const uint32_t nchunks = ((vocab / 4u) * 4u + kChunk - 1) / kChunk;
-    // The merged records (at most kCap / splits entries each) must fit one
-    // candidate list and still hold k plus ties.
-    uint32_t max_splits = kCap / (top_k + RSC_SHARD_TIE_CAP);
-    if (max_splits > kMaxSplits) max_splits = kMaxSplits;
-    if (max_splits > nchunks) max_splits = nchunks;
-    uint32_t s = static_cast<uint32_t>(ctas / rows);
-    if (s > max_splits) s = max_splits;
-    while (s > 1 && rows * s > max_units) --s;
-    return s < 1 ? 1u : s;
+    uint32_t nch = (vocab + kChunk - 1) / kChunk;
+    if (nch == 0) nch = 1;
+    StreamPlan pl;
+    pl.nch = nch;
+    pl.streamk = 0;
+    pl.max_parts = 1;
+    pl.grid = static_cast<uint32_t>(rows < ctas ? rows : ctas);
+    // Balanced ranges need top-k (a part's record keeps k + ties) and rows of
+    // more than one chunk; otherwise whole rows go round-robin.
+    if (rows == 0 || !topk_active || nch < 2) return pl;
+    uint32_t pmax = kCap / (top_k + RSC_SHARD_TIE_CAP);
+    if (pmax > kMaxSplits) pmax = kMaxSplits;
+    if (pmax < 2) return pl;
+    const unsigned long long T = static_cast<unsigned long long>(rows) * nch;
+    unsigned long long G = T < ctas ? T : ctas;
+    uint32_t parts;
+    if (rows <= 4096) {
+        // Exact: the most CTAs any row is spread over, for this grid; fewer
+        // CTAs until the rows' merged records fit one candidate list.
+        auto owner = [&](unsigned long long x, unsigned long long g) {
+            return ((x + 1ull) * g - 1ull) / T;
+        };
+        for (;; --G) {
+            unsigned long long most = 1;
+            for (size_t r = 0; r < rows; ++r) {
+                const unsigned long long a = static_cast<unsigned long long>(r) * nch;
+                const unsigned long long n = owner(a + nch - 1ull, G) - owner(a, G) + 1ull;
+                if (n > most) most = n;
+            }
+            if (most <= pmax || G == 1) {
+                parts = static_cast<uint32_t>(most);
+                break;
+            }
+        }
+    } else {
+        // Every CTA's range spans at least R = floor(T / G) chunks, so a row
+        // is cut by at most (nch - 2) / R + 1 range ends.
+        unsigned long long R = T / G;
+        if ((nch - 2ull) / R + 2ull > pmax) {
+            G = T / ((nch - 2ull) / (pmax - 1ull) + 1ull);
+            if (G < 1) G = 1;
+            R = T / G;
+        }
+        parts = static_cast<uint32_t>((nch - 2ull) / R + 2ull);
+        if (parts > nch) parts = nch;
+    }
+    if (parts > pmax) return pl;
+    if (static_cast<unsigned long long>(rows) * parts * split_record_bytes(parts) > seg_capacity_bytes)
+        return pl;
+    pl.streamk = 1;
+    pl.grid = static_cast<uint32_t>(G);
+    pl.max_parts = parts;
+    return pl;
 }
 
 cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                size_t row_stride, const CallParams &p, uint32_t *out_ids,
                                int32_t *out_status, float *out_probs, uint32_t *large_rows,
-                               uint32_t *large_count, uint32_t splits, void *seg_records,
-                               uint32_t *row_arrivals, int num_sms, cudaStream_t stream) {
+                               uint32_t *large_count, const StreamPlan &plan, void *seg_records,
+                               uint32_t *row_arrivals, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
     cudaError_t e = prepare(stream_topk_kernel<false>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
-    if (splits < 1 || !p.topk_active) splits = 1;
-    const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
-    const size_t units = rows * splits;
-    const size_t grid = units < ctas ? units : ctas;
-    stream_topk_kernel<false><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
+    stream_topk_kernel<false><<<plan.grid, kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
-        large_count, 0u, nullptr, split_record_bytes(splits), splits,
-        static_cast<unsigned char *>(seg_records), row_arrivals);
+        large_count, 0u, nullptr, split_record_bytes(plan.max_parts), plan.nch, plan.streamk,
+        plan.max_parts, static_cast<unsigned char *>(seg_records), row_arrivals);
     return cudaGetLastError();
 }
 
@@ -1159,9 +1223,11 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
     if (e != cudaSuccess) return e;
     const size_t ctas = static_cast<size_t>(num_sms) * kCtasPerSm;
     const size_t grid = rows < ctas ? rows : ctas;
+    const uint32_t nch = shard_vocab ? (shard_vocab + kChunk - 1) / kChunk : 1u;
     stream_topk_kernel<true><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
         logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, nullptr,
-        shard_offset, static_cast<unsigned char *>(records), rec_bytes, 1u, nullptr, nullptr);
+        shard_offset, static_cast<unsigned char *>(records), rec_bytes, nch, 0u, 1u, nullptr,
+        nullptr);
     return cudaGetLastError();
 }
 
