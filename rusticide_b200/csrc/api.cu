@@ -20,9 +20,8 @@ struct rsc_sampler {
     size_t max_vocab = 0;
     int num_sms = 0;
     uint32_t large_slots = 0;
-    uint32_t *large_rows = nullptr;   // [max_rows]
-    uint32_t *large_count = nullptr;  // [2]: list length, drain exit count
     uint32_t *scratch = nullptr;      // [large_slots][4 * max_vocab]
+    uint32_t *slot_lock = nullptr;    // [large_slots], zero when a slot is free
     size_t max_units = 0;             // row segments of the streaming kernel
     rsc::StreamPlan plan{};           // schedule of the last streaming call
     size_t plan_rows = 0;
@@ -96,6 +95,16 @@ rsc::CallParams make_params(const rsc_params &p, size_t vocab, const float *unif
     return cp;
 }
 
+// The per-row arrays of `cp` from row r0 on (a batch of a larger call).
+rsc::CallParams rows_from(const rsc::CallParams &cp, size_t r0) {
+    rsc::CallParams b = cp;
+    if (b.uniforms) b.uniforms += r0;
+    if (b.rng_states) b.rng_states += r0;
+    if (b.out_nsurv) b.out_nsurv += r0;
+    if (b.out_surv) b.out_surv += r0 * b.surv_cap;
+    return b;
+}
+
 rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t vocab,
                        size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
                        int32_t *status, float *probs, cudaStream_t stream) {
@@ -106,28 +115,32 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
                         (!cp.topk_active && vocab <= rsc::kSmallCap));
     cudaError_t e;
     if (small) {
-        // large_count is zero here: the draining kernel resets it.
-        if (!s->plan_valid || s->plan_rows != rows || s->plan_vocab != v ||
-            s->plan_topk != (cp.topk_active ? cp.top_k : 0u)) {
-            s->plan = rsc::stream_plan(rows, v, cp.topk_active, cp.top_k, s->num_sms,
-                                       s->max_units * rsc::split_record_bytes(2));
-            s->plan_rows = rows;
-            s->plan_vocab = v;
-            s->plan_topk = cp.topk_active ? cp.top_k : 0u;
-            s->plan_valid = true;
+        // One launch per batch of at most kStreamRowsPerCta rows per CTA (a
+        // single launch for every batch that fits the GPU this many times).
+        const size_t batch = static_cast<size_t>(s->num_sms) * 3u * rsc::kStreamRowsPerCta;
+        for (size_t r0 = 0; r0 < rows; r0 += batch) {
+            const size_t nr = rows - r0 < batch ? rows - r0 : batch;
+            if (!s->plan_valid || s->plan_rows != nr || s->plan_vocab != v ||
+                s->plan_topk != (cp.topk_active ? cp.top_k : 0u)) {
+                s->plan = rsc::stream_plan(nr, v, cp.topk_active, cp.top_k, s->num_sms,
+                                           s->max_units * rsc::split_record_bytes(2));
+                s->plan_rows = nr;
+                s->plan_vocab = v;
+                s->plan_topk = cp.topk_active ? cp.top_k : 0u;
+                s->plan_valid = true;
+            }
+            const rsc::CallParams bp = rows_from(cp, r0);
+            e = rsc::launch_stream_topk(logits + r0 * row_stride, nr, v, row_stride, bp, ids + r0,
+                                        status + r0, probs ? probs + r0 : nullptr, s->plan,
+                                        s->seg_records, s->row_arrivals, s->scratch, s->large_slots,
+                                        s->slot_lock, stream);
+            ++s->launches;
+            if (e != cudaSuccess) return RSC_ERR_CUDA;
         }
-        e = rsc::launch_stream_topk(logits, rows, v, row_stride, cp, ids, status, probs,
-                                    s->large_rows, s->large_count, s->plan, s->seg_records,
-                                    s->row_arrivals, stream);
-        ++s->launches;
-        if (e != cudaSuccess) return RSC_ERR_CUDA;
-        e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->large_rows,
-                              s->large_count, s->scratch, s->large_slots, stream);
-        ++s->launches;
-        return cuda_status(e);
+        return RSC_OK;
     }
-    e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, nullptr, nullptr,
-                          s->scratch, s->large_slots, stream);
+    e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
+                          s->large_slots, stream);
     ++s->launches;
     return cuda_status(e);
 }
@@ -184,9 +197,8 @@ rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab, rsc
     size_t slots = static_cast<size_t>(s->num_sms);
     if (slots > s->max_rows) slots = s->max_rows;
     s->large_slots = static_cast<uint32_t>(slots);
-    if (e == cudaSuccess) e = cudaMalloc(&s->large_rows, s->max_rows * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMalloc(&s->large_count, 2 * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(s->large_count, 0, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&s->slot_lock, s->large_slots * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(s->slot_lock, 0, s->large_slots * sizeof(uint32_t));
     if (e == cudaSuccess)
         e = cudaMalloc(&s->scratch, static_cast<size_t>(s->large_slots) * 4u * s->max_vocab *
                                         sizeof(uint32_t));
@@ -216,8 +228,7 @@ rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab, rsc
 rsc_status rsc_sampler_destroy(rsc_sampler *s) {
     if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
     DeviceGuard guard(s->device);
-    cudaFree(s->large_rows);
-    cudaFree(s->large_count);
+    cudaFree(s->slot_lock);
     cudaFree(s->scratch);
     cudaFree(s->seg_records);
     cudaFree(s->row_arrivals);

@@ -106,7 +106,7 @@ extern "C" RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t r
     if (slots > static_cast<size_t>(s->num_sms)) slots = static_cast<size_t>(s->num_sms);
     if (slots > rows) slots = rows;
     cudaError_t e = rsc::launch_large(d_logits, rows, static_cast<uint32_t>(vocab), row_stride, cp,
-                                      d_out_ids, d_out_status, d_out_probs, nullptr, nullptr,
+                                      d_out_ids, d_out_status, d_out_probs,
                                       s->scratch, static_cast<uint32_t>(slots),
                                       static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? RSC_OK : RSC_ERR_CUDA;

@@ -58,34 +58,6 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) {
     return s > kSat ? kSat : s;
 }
 
-// Exclusive block scan of saturating sums; returns the thread's exclusive
-// prefix and writes the block total to *total.
-template <int THREADS>
-__device__ __forceinline__ uint32_t block_exclusive_sat(uint32_t v, uint32_t *red, uint32_t *total) {
-    constexpr int W = THREADS / 32;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl = sat_add(incl, n);
-    }
-    __syncthreads();
-    if (lane == 31) red[warp] = incl;
-    __syncthreads();
-    uint32_t before = 0, all = 0;
-#pragma unroll
-    for (int w = 0; w < W; ++w) {
-        uint32_t x = red[w];
-        if (w < warp) before = sat_add(before, x);
-        all = sat_add(all, x);
-    }
-    *total = all;
-    uint32_t excl_in_warp = __shfl_up_sync(0xffffffffu, incl, 1);
-    if (lane == 0) excl_in_warp = 0;
-    return sat_add(before, excl_in_warp);
-}
-
 // Plain (non-saturating) exclusive block scan of counts.
 template <int THREADS>
 __device__ __forceinline__ uint32_t block_exclusive_add(uint32_t v, uint32_t *red, uint32_t *total) {
@@ -238,23 +210,8 @@ __device__ uint32_t block_select_kth_largest(uint32_t count, uint32_t k, Get get
 // ---------------------------------------------------------------------------
 // Exact parallel replay of a sequential binary32 sum s <- fl(s + t_j), j in
 // order, over non-negative terms (NaN allowed), as the reference's fold and
-// running sums compute it (src/candidates.rs:66-75, src/filters.rs:8,
+// running sums compute them (src/candidates.rs:66-75, src/filters.rs:8,
 // src/sampler.rs:113-119).
-//
-// While s stays inside one binade [2^E, 2^(E+1)) (E >= -126; the subnormal
-// range counts as one binade with the same spacing), every representable s is
-// an integer multiple S of u = 2^(E-23), S < 2^24, and fl(s + t) is S + q + up
-// where t/u = q + f, up = (f > 1/2): an integer sum, which a block scan adds
-// up exactly. The model breaks at a "barrier": a term whose rounding is a tie
-// (f = 1/2, where the result depends on the parity of the running S), a term
-// of at least 2^(E+1), a NaN, or the first step whose exact sum leaves the
-// binade (S + P_j + q_j >= 2^24). At a barrier the step is done as one real
-// binary32 add, the binade is re-derived, and the scan restarts after it.
-// Results are bit-identical to the sequential loop.
-//
-// Terms come from term(j) for j in [0, n). pred(s_after) is a stop
-// predicate: the replay returns the first j whose running sum after adding
-// t_j satisfies it (or stop = -1 and the full sum).
 // ---------------------------------------------------------------------------
 struct ReplayResult {
     float sum;     // full sum (stop < 0), else undefined
@@ -263,134 +220,197 @@ struct ReplayResult {
     float after;   // running sum after t_stop
 };
 
-struct ReplaySmem {
-    uint32_t red[32];
-    uint32_t total;
-    uint32_t ev;
-    uint32_t pr;
-    float s_new;
-    float s_before;
-    float s_after;
-    int stop_flag;
-};
-
 constexpr uint32_t kNoPos = 0xffffffffu;
 
+// The float S * u of binade Ef (S up to 2^24, which is 2^(E+1)).
 __device__ __forceinline__ float replay_make(uint32_t S, uint32_t Ef) {
     return __uint_as_float(((Ef - 1u) << 23) + S);
 }
 
+// The model: while s stays inside one binade [2^E, 2^(E+1)) (E >= -126; the
+// subnormal range counts as one binade with the same spacing), every
+// representable s is S * u with u = 2^(E-23), S < 2^24, and a term t with
+// t/u = q + f adds q, plus 1 when f > 1/2. Two further facts make it parallel:
+//  - A tie (t/u = q + 1/2) is no barrier. Round-half-to-even makes the step
+//    S -> S + q + ((S + q) & 1): its increment depends only on the parity of
+//    S. So a run of steps maps S to S + delta[S & 1], a pair of increments
+//    for even and odd S, and pairs compose associatively; a block scan of
+//    pairs replays ties exactly, in order.
+//  - The running sum never decreases (terms >= +0), so a tile whose total
+//    stays inside the binade and does not satisfy the (monotone) stop
+//    predicate needs no per-element search; only the rare tile with an event
+//    (binade exit, term of the next binade or above, NaN, or the stop) is
+//    searched, and the event step is done as one real binary32 add.
+// Terms come from a functor with prepare(tmin), called once per tile with
+// tmin = u/2 of the tile's starting binade (any term below it rounds away
+// for the rest of the tile, since u only grows), load(j) (a plain read) and
+// eval(j, loaded) (the term).
+// ---------------------------------------------------------------------------
+struct ReplayPair {
+    uint32_t d0, d1;  // increment of S for even S, for odd S
+};
+
+// `a` then `b`.
+__device__ __forceinline__ ReplayPair rp_compose(ReplayPair a, ReplayPair b) {
+    ReplayPair r;
+    r.d0 = sat_add(a.d0, (a.d0 & 1u) ? b.d1 : b.d0);
+    r.d1 = sat_add(a.d1, (a.d1 & 1u) ? b.d0 : b.d1);
+    return r;
+}
+
+// The step of term t in the binade with exponent field Ef (>= 1). NaN, and
+// terms of binade Ef + 1 or above, saturate (always an event).
+__device__ __forceinline__ ReplayPair rp_term(float tv, uint32_t Ef) {
+    const uint32_t tb = __float_as_uint(tv);
+    if ((tv != tv) || (tb >> 31)) return ReplayPair{kSat, kSat};
+    const uint32_t tf = tb >> 23;
+    const uint32_t mt = tf ? ((tb & 0x7fffffu) | 0x800000u) : (tb & 0x7fffffu);
+    const int shift = static_cast<int>(Ef) - static_cast<int>(max(tf, 1u));
+    if (shift < 0) return ReplayPair{kSat, kSat};
+    if (shift == 0) return ReplayPair{mt, mt};
+    if (shift >= 25) return ReplayPair{0u, 0u};
+    const uint32_t q = mt >> shift;
+    const uint32_t rem = mt & ((1u << shift) - 1u);
+    const uint32_t half = 1u << (shift - 1);
+    if (rem > half) return ReplayPair{q + 1u, q + 1u};
+    if (rem < half) return ReplayPair{q, q};
+    return ReplayPair{q + (q & 1u), q + 1u - (q & 1u)};
+}
+
+__device__ __forceinline__ uint32_t rp_apply(ReplayPair p, uint32_t S) {
+    return sat_add(S, (S & 1u) ? p.d1 : p.d0);
+}
+
+struct ReplaySmem {
+    ReplayPair wsm[33];
+    uint32_t red[32];
+    float s_before;
+    float s_new;
+    int stop_flag;
+};
+
+// Exclusive block scan of pairs (in thread order); *total gets the whole
+// block's composition. Ends with wsm free for reuse.
+template <int THREADS>
+__device__ __forceinline__ ReplayPair block_exclusive_pairs(ReplayPair v, ReplaySmem &sm,
+                                                            ReplayPair *total) {
+    constexpr int W = THREADS / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    ReplayPair inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        ReplayPair up{__shfl_up_sync(0xffffffffu, inc.d0, o), __shfl_up_sync(0xffffffffu, inc.d1, o)};
+        if (lane >= o) inc = rp_compose(up, inc);
+    }
+    ReplayPair ex{__shfl_up_sync(0xffffffffu, inc.d0, 1), __shfl_up_sync(0xffffffffu, inc.d1, 1)};
+    if (lane == 0) ex = ReplayPair{0u, 0u};
+    if (lane == 31) sm.wsm[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        ReplayPair w = lane < W ? sm.wsm[lane] : ReplayPair{0u, 0u};
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            ReplayPair up{__shfl_up_sync(0xffffffffu, w.d0, o), __shfl_up_sync(0xffffffffu, w.d1, o)};
+            if (lane >= o) w = rp_compose(up, w);
+        }
+        ReplayPair wex{__shfl_up_sync(0xffffffffu, w.d0, 1), __shfl_up_sync(0xffffffffu, w.d1, 1)};
+        if (lane == 0) wex = ReplayPair{0u, 0u};
+        __syncwarp();
+        if (lane < W) sm.wsm[lane] = wex;
+        if (lane == W - 1) sm.wsm[32] = w;
+    }
+    __syncthreads();
+    const ReplayPair r = rp_compose(sm.wsm[warp], ex);
+    *total = sm.wsm[32];
+    __syncthreads();
+    return r;
+}
+
 template <int THREADS, int ITEMS, typename Term, typename Pred>
-__device__ ReplayResult block_replay(uint32_t n, Term term, Pred pred, ReplaySmem &sm) {
+__device__ ReplayResult block_replay(uint32_t n, Term &term, Pred pred, ReplaySmem &sm) {
     constexpr uint32_t CH = THREADS * ITEMS;
+    constexpr uint32_t kTop = 1u << 24;
     const uint32_t tid = threadIdx.x;
     float s = 0.0f;
     for (uint32_t base = 0; base < n; base += CH) {
+        if (s != s) return ReplayResult{s, -1, s, s};  // NaN stays NaN; no predicate fires
+        {
+            const uint32_t Ef0 = max(__float_as_uint(s) >> 23, 1u);
+            // u/2 = 2^(Ef - 151); below 2^-149 nothing rounds away.
+            term.prepare(__uint_as_float(Ef0 << 23) * 0x1p-24f);
+        }
         float t[ITEMS];
 #pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {  // loads first, all in flight together
+            const uint32_t j = base + tid * ITEMS + i;
+            t[i] = j < n ? term.load(j) : 0.0f;
+        }
+#pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
-            uint32_t j = base + tid * ITEMS + i;
-            t[i] = j < n ? term(j) : 0.0f;
+            const uint32_t j = base + tid * ITEMS + i;
+            t[i] = j < n ? term.eval(j, t[i]) : 0.0f;
         }
         uint32_t start = 0;
         while (true) {
-            if (s != s) return ReplayResult{s, -1, s, s};  // NaN stays NaN; no predicate fires
+            if (s != s) return ReplayResult{s, -1, s, s};
             const uint32_t sb = __float_as_uint(s);
             const uint32_t Ef = max(sb >> 23, 1u);
-            const uint32_t S = (sb >> 23) ? ((sb & 0x7fffffu) | 0x800000u) : (sb & 0x7fffffu);
-            uint32_t d[ITEMS], q[ITEMS];
-            uint32_t ev_local = kNoPos;
-            uint32_t acc = 0;
+            const uint32_t S0 = (sb >> 23) ? ((sb & 0x7fffffu) | 0x800000u) : (sb & 0x7fffffu);
+            ReplayPair pr[ITEMS];
+            ReplayPair acc{0u, 0u};
 #pragma unroll
             for (int i = 0; i < ITEMS; ++i) {
                 const uint32_t pos = tid * ITEMS + i;
-                d[i] = 0;
-                q[i] = 0;
-                if (pos >= start) {
-                    const float tv = t[i];
-                    const uint32_t tb = __float_as_uint(tv);
-                    const uint32_t tf = tb >> 23;  // terms are >= +0 or NaN (sign 0 or NaN)
-                    bool barrier = (tv != tv) || (tb >> 31);
-                    const uint32_t mt = tf ? ((tb & 0x7fffffu) | 0x800000u) : (tb & 0x7fffffu);
-                    const int shift = static_cast<int>(Ef) - static_cast<int>(max(tf, 1u));
-                    if (shift < 0) {
-                        barrier = true;
-                    } else if (shift == 0) {
-                        q[i] = mt;
-                    } else if (shift < 25) {
-                        const uint32_t qq = mt >> shift;
-                        const uint32_t rem = mt & ((1u << shift) - 1u);
-                        const uint32_t half = 1u << (shift - 1);
-                        q[i] = qq;
-                        d[i] = (rem > half) ? 1u : 0u;
-                        if (rem == half) barrier = true;
-                    }
-                    d[i] += q[i];
-                    if (barrier) {
-                        ev_local = min(ev_local, pos);
-                        d[i] = 0;
-                        q[i] = 0;
-                    }
+                pr[i] = ReplayPair{0u, 0u};
+                // +0 terms (skipped or filtered positions) leave S unchanged.
+                if (pos >= start && base + pos < n && __float_as_uint(t[i]) != 0u) {
+                    pr[i] = rp_term(t[i], Ef);
+                    acc = rp_compose(acc, pr[i]);
                 }
-                acc = sat_add(acc, d[i]);
             }
-            uint32_t total;
-            const uint32_t excl = block_exclusive_sat<THREADS>(acc, sm.red, &total);
-            // First step whose exact sum leaves the binade: S + P_j + q_j >= 2^24.
-            uint32_t run = excl;
+            ReplayPair total;
+            const ReplayPair ex = block_exclusive_pairs<THREADS>(acc, sm, &total);
+            const uint32_t S_end = rp_apply(total, S0);
+            if (S_end < kTop && !pred(replay_make(S_end, Ef))) {
+                s = replay_make(S_end, Ef);
+                break;
+            }
+            // The first event of the tile: a step leaving the binade (or a
+            // saturated one), or the first sum satisfying the predicate.
+            uint32_t S = rp_apply(ex, S0);
+            uint32_t ev_local = kNoPos;
 #pragma unroll
             for (int i = 0; i < ITEMS; ++i) {
                 const uint32_t pos = tid * ITEMS + i;
-                if (pos >= start && S + run + q[i] >= (1u << 24)) ev_local = min(ev_local, pos);
-                run = sat_add(run, d[i]);
+                if (ev_local == kNoPos && pos >= start && base + pos < n) {
+                    const uint32_t after = rp_apply(pr[i], S);
+                    if (after >= kTop || pred(replay_make(after, Ef))) ev_local = pos;
+                    S = after;
+                }
             }
             const uint32_t ev = block_reduce<THREADS>(ev_local, sm.red, OpMinU32());
-            // Predicate on the modelled steps before the event.
-            uint32_t pr_local = kNoPos;
-            run = excl;
-#pragma unroll
-            for (int i = 0; i < ITEMS; ++i) {
-                const uint32_t pos = tid * ITEMS + i;
-                const uint32_t after = sat_add(run, d[i]);
-                if (pos >= start && pos < ev && base + pos < n && pr_local == kNoPos &&
-                    pred(replay_make(S + after, Ef)))
-                    pr_local = pos;
-                run = after;
+            if (ev == kNoPos) {  // not reached: the total saw an event
+                s = replay_make(min(S_end, kTop), Ef);
+                break;
             }
-            const uint32_t pr = block_reduce<THREADS>(pr_local, sm.red, OpMinU32());
-            if (pr != kNoPos) {
-                run = excl;
+            if (ev_local == ev) {
+                // Its owner redoes the walk up to the event.
+                uint32_t Sb = rp_apply(ex, S0);
 #pragma unroll
                 for (int i = 0; i < ITEMS; ++i) {
                     const uint32_t pos = tid * ITEMS + i;
-                    if (pos == pr) {
-                        sm.s_before = replay_make(S + run, Ef);
-                        sm.s_after = replay_make(S + run + d[i], Ef);
+                    if (pos >= start && pos < ev) Sb = rp_apply(pr[i], Sb);
+                    if (pos == ev) {
+                        const float before = replay_make(Sb, Ef);
+                        const uint32_t Sa = rp_apply(pr[i], Sb);
+                        float after;
+                        if (Sa >= kTop) after = __fadd_rn(before, t[i]);  // the real step
+                        else after = replay_make(Sa, Ef);
+                        sm.s_before = before;
+                        sm.s_new = after;
+                        sm.stop_flag = pred(after) ? 1 : 0;
                     }
-                    run = sat_add(run, d[i]);
                 }
-                __syncthreads();
-                ReplayResult r{0.0f, static_cast<long long>(base + pr), sm.s_before, sm.s_after};
-                __syncthreads();
-                return r;
-            }
-            if (ev == kNoPos) {
-                s = replay_make(S + total, Ef);
-                break;
-            }
-            // The event step, done as one binary32 add by its owner.
-            run = excl;
-#pragma unroll
-            for (int i = 0; i < ITEMS; ++i) {
-                const uint32_t pos = tid * ITEMS + i;
-                if (pos == ev) {
-                    const float before = replay_make(S + run, Ef);
-                    const float after = __fadd_rn(before, t[i]);
-                    sm.s_before = before;
-                    sm.s_new = after;
-                    sm.stop_flag = (base + pos < n && pred(after)) ? 1 : 0;
-                }
-                run = sat_add(run, d[i]);
             }
             __syncthreads();
             const float s_new = sm.s_new, s_before = sm.s_before;

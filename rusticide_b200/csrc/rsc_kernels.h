@@ -23,6 +23,12 @@ cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size
 // Most CTAs a row is spread over by the streaming kernel.
 constexpr uint32_t kStreamMaxSplits = 16;
 
+// Overflowing rows one streaming CTA can defer to its epilogue; a launch
+// covers at most kStreamRowsPerCta rows per CTA so that the list never fills
+// (a CTA's pieces span at most rows / grid + 3 rows).
+constexpr uint32_t kStreamOvfCap = 64;
+constexpr uint32_t kStreamRowsPerCta = 48;
+
 // Bytes of one part record when a row is spread over `parts` CTAs (kSmallCap /
 // parts entries).
 size_t split_record_bytes(uint32_t parts);
@@ -43,27 +49,26 @@ struct StreamPlan {
 StreamPlan stream_plan(size_t rows, uint32_t vocab, bool topk_active, uint32_t top_k,
                        int num_sms, size_t seg_capacity_bytes);
 
-// Streaming top-k kernel for rows whose survivors fit kSmallCap. Rows that
-// overflow are appended to large_rows[large_count[0]]. A row spread over
-// several CTAs leaves one record per part in seg_records (rows * max_parts
-// records of split_record_bytes(max_parts)); row_arrivals (rows counters,
-// zero on entry and on exit) tells the last part to merge them.
+// Streaming top-k kernel for rows whose survivors fit kSmallCap, launched as
+// a programmatic dependent of the previous work on the stream (it writes
+// global memory only after that work completes). A row spread over several
+// CTAs leaves one record per part in seg_records (rows * max_parts records of
+// split_record_bytes(max_parts)); row_arrivals (rows counters, zero on entry
+// and on exit) tells the last part to merge them. Rows whose candidates
+// overflow are sampled at the end of their CTA with the large-row code, in a
+// scratch slot (`slots` regions of 4 * vocab uint32) taken under slot_lock
+// (`slots` words, zero when free). rows <= plan.grid * kStreamRowsPerCta.
 cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                size_t row_stride, const CallParams &p, uint32_t *out_ids,
-                               int32_t *out_status, float *out_probs, uint32_t *large_rows,
-                               uint32_t *large_count, const StreamPlan &plan, void *seg_records,
-                               uint32_t *row_arrivals, cudaStream_t stream);
+                               int32_t *out_status, float *out_probs, const StreamPlan &plan,
+                               void *seg_records, uint32_t *row_arrivals, uint32_t *scratch,
+                               uint32_t slots, uint32_t *slot_lock, cudaStream_t stream);
 
-// Large-survivor kernel. With large_rows == nullptr it processes rows
-// [0, rows); otherwise the rows listed in large_rows[0 .. large_count[0]),
-// launched as a programmatic dependent of the streaming kernel, and it resets
-// large_count[0..1] to zero when done.
+// Large-survivor kernel over rows [0, rows), one 512-thread block per row.
 // Scratch: `slots` regions of 4 * vocab uint32 each.
 cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
-                         float *out_probs, const uint32_t *large_rows,
-                         uint32_t *large_count, uint32_t *scratch, uint32_t slots,
-                         cudaStream_t stream);
+                         float *out_probs, uint32_t *scratch, uint32_t slots, cudaStream_t stream);
 
 // Vocab-sharded record: this header, then uint32 key[k + RSC_SHARD_TIE_CAP]
 // and uint32 index[k + RSC_SHARD_TIE_CAP] (global indices), entries sorted by

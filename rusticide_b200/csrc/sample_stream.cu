@@ -24,13 +24,13 @@
 //    one lane in the reference's order, so every result is bit-identical.
 //
 // Rows whose list overflows kCap (thousands of logits tied with the k-th) are
-// handed to the large-survivor kernel through a device list.
+// kept in a per-CTA list and sampled at the end of the CTA by all its threads
+// with the large-row code (rsc_large.cuh), so a call is one launch.
 //
 // All waits are bounded (mbar_wait); the consumer warps decide together
 // through barrier reductions, so a timeout can never leave some of them at a
 // barrier the others have left.
-#include "rsc_block.cuh"
-#include "rsc_kernels.h"
+#include "rsc_large.cuh"
 
 namespace rsc {
 
@@ -48,6 +48,7 @@ constexpr uint32_t kCap = kSmallCap;  // candidate list capacity
 constexpr uint32_t kCompactAt = kCap / 2;
 constexpr int kBarConsumers = 1;      // named barrier of the consumer warps
 constexpr uint32_t kMaxSplits = kStreamMaxSplits;
+constexpr uint32_t kOvfCap = kStreamOvfCap;  // overflowing rows a CTA can defer
 static_assert(kSmallTopK <= 8 * 32, "tau uses the t-th of 32 lane maxima per warp, t = ceil(k/8)");
 static_assert(kSmallTopK <= kCompactAt / 2, "the list must hold k plus a chunk's new candidates");
 
@@ -89,7 +90,12 @@ struct StreamSmem {
     uint32_t csel[2];
     uint32_t error;
     uint32_t issued;
+    uint32_t ovf_count;  // rows deferred to the epilogue (finisher only)
+    uint32_t ovf_rows[kOvfCap];
+    uint32_t slot;
 };
+static_assert(sizeof(large::LargeSmem<kThreads>) <= sizeof(float) * kStages * kChunk,
+              "the epilogue's large-row workspace lives in the idle ring");
 
 // Geometry of one row: a scalar head up to 16-byte alignment, a body of
 // `nbody` logits copied by TMA in chunks, a scalar tail.
@@ -734,6 +740,28 @@ __device__ __forceinline__ bool get_piece(size_t rows, uint32_t nch, uint32_t st
     return true;
 }
 
+// A row whose candidates overflowed joins the CTA's epilogue list (one lane
+// of the finisher). The host bounds the rows per CTA below kOvfCap; a full
+// list would report the row as not sampled.
+__device__ __forceinline__ void defer_row(StreamSmem &sm, size_t row, uint32_t *out_ids,
+                                          int32_t *out_status) {
+    if (sm.ovf_count < kOvfCap) {
+        sm.ovf_rows[sm.ovf_count++] = static_cast<uint32_t>(row);
+    } else {
+        out_ids[row] = 0;
+        out_status[row] = RSC_ROW_INTERNAL;
+    }
+}
+
+// The epilogue's per-row work, kept out of line so that the large-row code's
+// register pressure stays out of the streaming loops.
+__device__ __noinline__ void epilogue_row(const CallParams &cp, const float *p, uint32_t vocab,
+                                          size_t row, uint32_t *scratch, uint32_t *out_ids,
+                                          int32_t *out_status, float *out_probs,
+                                          large::LargeSmem<kThreads> &ls) {
+    large::sample_row<kThreads>(cp, p, vocab, row, scratch, out_ids, out_status, out_probs, ls);
+}
+
 // --- the streaming kernel -------------------------------------------------------
 
 template <bool kRecord>
@@ -741,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab,
                    size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs,
-                   uint32_t *__restrict__ large_rows, uint32_t *__restrict__ large_count,
+                   uint32_t *__restrict__ scratch, uint32_t slots, uint32_t *__restrict__ slot_lock,
                    uint32_t index_offset, unsigned char *__restrict__ records, size_t rec_bytes,
                    uint32_t nch, uint32_t streamk, uint32_t max_parts,
                    unsigned char *__restrict__ seg_records, uint32_t *__restrict__ row_arrivals) {
@@ -766,15 +794,191 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         }
         sm.error = 0;
         sm.issued = 0;
+        sm.ovf_count = 0;
         fence_barrier_init();
     }
-    __syncthreads();  // the last block-wide barrier: the roles split here
-    // The kernel that drains overflowing rows may start launching now; it
-    // waits for this grid's completion before reading the list.
+    __syncthreads();  // the roles split here and meet again in the epilogue
+    // A programmatic dependent launch of the next call may start now: its
+    // CTAs stream logits (read only) as this grid's CTAs retire, and wait for
+    // this grid's completion before they write anything to global memory.
     if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;");
 
+    // Consumers: warps 0 .. kConsumerWarps-1 (a consumer that leaves early
+    // does not wait for the others: the finisher's and producer's bounded
+    // waits end their roles, and every role meets in the epilogue).
+    auto consume = [&]() {
+        const int cw = warp;
+        const float scale = cp.scale;
+        const uint32_t t_bound = cp.topk_active ? (cp.top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
+        uint32_t consumed = 0, par = 0;
+        Piece pc;
+        for (uint32_t j = 0; get_piece(rows, nch, streamk, j, pc); ++j) {
+            const size_t row = pc.row;
+            const uint32_t b = j & 1u;
+            bool bad = false;
+            if (threadIdx.x == 0) {
+                if (j >= 2 && !mbar_wait(&sm.list_empty[b], ((j >> 1) - 1u) & 1u)) bad = true;
+                sm.count[b] = 0;
+                sm.overflow[b] = 0;
+            }
+            if (consumers_any(bad || *static_cast<volatile uint32_t *>(&sm.error) != 0)) break;
+            CandList &L = sm.list[b];
+            uint32_t *count = &sm.count[b];
+            uint32_t *ovf = &sm.overflow[b];
+            const RowGeom g = row_geom(logits, row, row_stride, vocab);
+            const uint32_t c0 = pc.c0;
+            const uint32_t c1 = min(pc.c1, g.nchunks);
+            // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
+            // NaN (NaN reads as -inf in the reference, and -inf never survives);
+            // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
+            float tau = -3.402823466e38f;
+            float lmax = kNegInf;  // this lane's largest scaled logit of the piece
+            // Scalar head and tail (at most 3 logits each).
+            {
+                const uint32_t ntail = vocab - g.head - g.nbody;
+                const uint32_t i = threadIdx.x;
+                uint32_t idx = ~0u;
+                if (pc.c0 == 0 && i < g.head) idx = i;
+                else if (pc.c1 == nch && i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
+                float v = kNegInf;
+                if (idx != ~0u) {
+                    v = __fmul_rn(g.p[idx], scale);
+                    lmax = fmaxf(lmax, v);
+                }
+                append_candidate(L, count, ovf, v >= tau, total_key(v), idx + index_offset, kCap);
+            }
+            bool stop = false;
+            bool got = true, mark = false;
+            for (uint32_t c = c0; c < c1; ++c) {
+                const uint32_t s = consumed % kStages;
+                got &= mbar_wait(&sm.full[s], (consumed / kStages) & 1u);
+                const uint32_t len = min(kChunk, g.nbody - c * kChunk);
+                const float4 *r4 = reinterpret_cast<const float4 *>(sm.ring[s]);
+                const uint32_t base_idx = g.head + c * kChunk + index_offset;
+                if (c == c0 && t_bound) {
+                    // First chunk: lane maxima before filtering, so that tau is
+                    // already high for this chunk's own logits.
+                    float cmr = kNegInf;
+    #pragma unroll
+                    for (uint32_t jj = 0; jj < kChunk / 4 / kConsumers; ++jj) {
+                        const uint32_t q = threadIdx.x + jj * kConsumers;
+                        if (4 * q < len) {
+                            const float4 f = r4[q];
+                            cmr = fmaxf(fmaxf(cmr, fmaxf(f.x, f.y)), fmaxf(f.z, f.w));
+                        }
+                    }
+                    lmax = fmaxf(lmax, __fmul_rn(cmr, scale));
+                    post_warp_bound(sm, lmax, t_bound, cw, par);
+                    if (consumers_any(!got)) {
+                        stop = true;
+                        break;
+                    }
+                    tau = fmaxf(tau, read_bound(sm, par));
+                    par ^= 1u;
+                }
+                constexpr uint32_t kPerThread = kChunk / 4 / kConsumers;
+                float4 f[kPerThread];
+                if (len == kChunk) {  // every chunk but a row's last
+    #pragma unroll
+                    for (uint32_t jj = 0; jj < kPerThread; ++jj) f[jj] = r4[threadIdx.x + jj * kConsumers];
+                } else {
+    #pragma unroll
+                    for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                        const uint32_t q = threadIdx.x + jj * kConsumers;
+                        f[jj] = (4 * q < len) ? r4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage s released by this warp
+                ++consumed;
+                // x -> fl(x * scale) is non-decreasing for a finite scale > 0, so
+                // the largest scaled value of a group of logits is the scaled
+                // largest raw value: one max per logit decides whether this
+                // thread's slice holds a candidate at all, and one max per float4
+                // which of its float4s do (fmaxf skips NaN, which reads as -inf).
+                float m4[kPerThread];
+    #pragma unroll
+                for (uint32_t jj = 0; jj < kPerThread; ++jj)
+                    m4[jj] = fmaxf(fmaxf(f[jj].x, f[jj].y), fmaxf(f[jj].z, f[jj].w));
+                float cmr = m4[0];
+    #pragma unroll
+                for (uint32_t jj = 1; jj < kPerThread; ++jj) cmr = fmaxf(cmr, m4[jj]);
+                const float cm = __fmul_rn(cmr, scale);
+                lmax = fmaxf(lmax, cm);
+                if (cm >= tau) {
+    #pragma unroll
+                    for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                        if (__fmul_rn(m4[jj], scale) >= tau) {
+                            const float v[4] = {__fmul_rn(f[jj].x, scale), __fmul_rn(f[jj].y, scale),
+                                                __fmul_rn(f[jj].z, scale), __fmul_rn(f[jj].w, scale)};
+                            const uint32_t m = (v[0] >= tau ? 1u : 0u) | (v[1] >= tau ? 2u : 0u) |
+                                               (v[2] >= tau ? 4u : 0u) | (v[3] >= tau ? 8u : 0u);
+                            mark |= append_mask(L, count, ovf, m, v,
+                                                base_idx + 4 * (threadIdx.x + jj * kConsumers), kCompactAt);
+                        }
+                    }
+                }
+                const bool last = c + 1 == c1;
+                // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
+                const uint32_t done = c + 1 - c0;
+                const bool refresh = last || (done < 8 ? (done & (done - 1)) == 0 && done > 1 : done % 8 == 0);
+                if (!refresh) continue;
+                if (t_bound) post_warp_bound(sm, lmax, t_bound, cw, par);
+                // One barrier per refresh: settles the list, publishes
+                // the bounds, and raises the rare events (a failed wait, a long
+                // list).
+                const bool want_compact = mark && cp.topk_active && !last;
+                mark = false;
+                if (consumers_any(!got || want_compact)) {
+                    if (consumers_any(!got)) {
+                        stop = true;
+                        break;
+                    }
+                    // Compaction: tau rises to the list's own k-th largest value.
+                    const uint32_t cnt = min(*count, kCap);
+                    if (cnt >= cp.top_k) {
+                        const uint32_t kth = group_select_kth_largest<kConsumers, ConsumerSync>(
+                            cnt, cp.top_k, [&](uint32_t i) { return L.key[i]; }, sm.chist, sm.csel);
+                        tau = fmaxf(tau, key_to_float(kth));
+                        constexpr int kPer = kCap / kConsumers;
+                        uint32_t kk[kPer], ii[kPer];
+    #pragma unroll
+                        for (int e = 0; e < kPer; ++e) {
+                            const uint32_t i = threadIdx.x + e * kConsumers;
+                            kk[e] = i < cnt ? L.key[i] : 0u;
+                            ii[e] = i < cnt ? L.idx[i] : 0u;
+                        }
+                        ConsumerSync::sync();
+                        if (threadIdx.x == 0) *count = 0;
+                        ConsumerSync::sync();
+    #pragma unroll
+                        for (int e = 0; e < kPer; ++e) {
+                            const uint32_t i = threadIdx.x + e * kConsumers;
+                            append_candidate(L, count, ovf, i < cnt && key_to_float(kk[e]) >= tau, kk[e],
+                                             ii[e], kCap);
+                        }
+                        ConsumerSync::sync();
+                        if (*count > kCompactAt && threadIdx.x == 0) *ovf = 1;
+                    }
+                }
+                if (t_bound) {
+                    tau = fmaxf(tau, read_bound(sm, par));
+                    par ^= 1u;
+                }
+            }
+            if (stop) break;
+            if (kRecord) {
+                const float wm = warp_max(lmax);
+                if (lane == 0) sm.st_max[b][cw] = wm;
+            }
+            if (threadIdx.x == 0) sm.tau_final[b] = tau;
+            ConsumerSync::sync();  // the row's list is complete
+            if (threadIdx.x == 0) mbar_arrive(&sm.list_full[b]);
+        }
+    };
+
     if (warp == kProducerWarp) {
-        if (lane != 0) return;
+      if (lane == 0) {
         uint32_t q = 0;
         bool ok = true;
         Piece pc;
@@ -798,14 +1002,15 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 ++q;
             }
         }
-        // Before this thread exits, every copy it issued has landed (bounded):
-        // the last phase of each stage.
+        // Before the ring is reused, every copy this thread issued has landed
+        // (bounded): the last phase of each stage.
         const uint32_t first = q > kStages ? q - kStages : 0u;
         for (uint32_t i = first; i < q; ++i) mbar_wait(&sm.full[i % kStages], (i / kStages) & 1u);
-        return;
-    }
-
-    if (warp == kFinisherWarp) {
+      }
+    } else if (warp == kFinisherWarp) {
+        // Global writes wait for the previous grid of the stream (a no-op
+        // unless this grid was launched as its programmatic dependent).
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         uint32_t u = 0;
         Piece pc;
         for (; get_piece(rows, nch, streamk, u, pc); ++u) {
@@ -837,7 +1042,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 }
             } else if (pc.nparts == 1) {
                 if (ov) {
-                    if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
+                    if (lane == 0) defer_row(sm, row, out_ids, out_status);
                 } else {
                     finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, cnt, cp, row,
                                 out_ids, out_status, out_probs);
@@ -870,7 +1075,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                         [&](uint32_t part) { return seg_records + (row * max_parts + part) * rec_bytes; },
                         pc.nparts, seg_cap, cp, &ok);
                     if (!ok) {
-                        if (lane == 0) large_rows[atomicAdd(large_count, 1u)] = static_cast<uint32_t>(row);
+                        if (lane == 0) defer_row(sm, row, out_ids, out_status);
                     } else {
                         finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, n, cp, row,
                                     out_ids, out_status, out_probs);
@@ -908,180 +1113,56 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             }
             __syncwarp();
         }
-        return;
+    } else {
+        consume();
     }
 
-    // Consumers: warps 0 .. kConsumerWarps-1.
-    const int cw = warp;
-    const float scale = cp.scale;
-    const uint32_t t_bound = cp.topk_active ? (cp.top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
-    uint32_t consumed = 0, par = 0;
-    Piece pc;
-    for (uint32_t j = 0; get_piece(rows, nch, streamk, j, pc); ++j) {
-        const size_t row = pc.row;
-        const uint32_t b = j & 1u;
-        bool bad = false;
+    // --- epilogue: the rows this CTA deferred ---------------------------------
+    // Every role is done and every copy into the ring has landed, so the ring
+    // holds the large-row workspace. The CTA takes a scratch slot (a bounded
+    // spin on a lock; holders never wait on anyone) and samples the rows one
+    // by one with all its threads.
+    __syncthreads();
+    if (!kRecord && sm.ovf_count > 0) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        large::LargeSmem<kThreads> &ls = *reinterpret_cast<large::LargeSmem<kThreads> *>(&sm.ring[0][0]);
+        load_exp_table(ls.exp_tab);
         if (threadIdx.x == 0) {
-            if (j >= 2 && !mbar_wait(&sm.list_empty[b], ((j >> 1) - 1u) & 1u)) bad = true;
-            sm.count[b] = 0;
-            sm.overflow[b] = 0;
-        }
-        if (consumers_any(bad || *static_cast<volatile uint32_t *>(&sm.error) != 0)) break;
-        CandList &L = sm.list[b];
-        uint32_t *count = &sm.count[b];
-        uint32_t *ovf = &sm.overflow[b];
-        const RowGeom g = row_geom(logits, row, row_stride, vocab);
-        const uint32_t c0 = pc.c0;
-        const uint32_t c1 = min(pc.c1, g.nchunks);
-        // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
-        // NaN (NaN reads as -inf in the reference, and -inf never survives);
-        // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
-        float tau = -3.402823466e38f;
-        float lmax = kNegInf;  // this lane's largest scaled logit of the piece
-        // Scalar head and tail (at most 3 logits each).
-        {
-            const uint32_t ntail = vocab - g.head - g.nbody;
-            const uint32_t i = threadIdx.x;
-            uint32_t idx = ~0u;
-            if (pc.c0 == 0 && i < g.head) idx = i;
-            else if (pc.c1 == nch && i >= 4 && i - 4 < ntail) idx = g.head + g.nbody + (i - 4);
-            float v = kNegInf;
-            if (idx != ~0u) {
-                v = __fmul_rn(g.p[idx], scale);
-                lmax = fmaxf(lmax, v);
-            }
-            append_candidate(L, count, ovf, v >= tau, total_key(v), idx + index_offset, kCap);
-        }
-        bool stop = false;
-        bool got = true, mark = false;
-        for (uint32_t c = c0; c < c1; ++c) {
-            const uint32_t s = consumed % kStages;
-            got &= mbar_wait(&sm.full[s], (consumed / kStages) & 1u);
-            const uint32_t len = min(kChunk, g.nbody - c * kChunk);
-            const float4 *r4 = reinterpret_cast<const float4 *>(sm.ring[s]);
-            const uint32_t base_idx = g.head + c * kChunk + index_offset;
-            if (c == c0 && t_bound) {
-                // First chunk: lane maxima before filtering, so that tau is
-                // already high for this chunk's own logits.
-                float cmr = kNegInf;
-#pragma unroll
-                for (uint32_t jj = 0; jj < kChunk / 4 / kConsumers; ++jj) {
-                    const uint32_t q = threadIdx.x + jj * kConsumers;
-                    if (4 * q < len) {
-                        const float4 f = r4[q];
-                        cmr = fmaxf(fmaxf(cmr, fmaxf(f.x, f.y)), fmaxf(f.z, f.w));
-                    }
-                }
-                lmax = fmaxf(lmax, __fmul_rn(cmr, scale));
-                post_warp_bound(sm, lmax, t_bound, cw, par);
-                if (consumers_any(!got)) {
-                    stop = true;
+            uint32_t got = ~0u;
+            const unsigned long long t0 = global_ns();
+            for (uint32_t i = 0; got == ~0u; ++i) {
+                const uint32_t s = (blockIdx.x + i) % slots;
+                if (atomicCAS(&slot_lock[s], 0u, 1u) == 0u) {
+                    got = s;
                     break;
                 }
-                tau = fmaxf(tau, read_bound(sm, par));
-                par ^= 1u;
+                if (global_ns() - t0 > kWaitLimitNs) break;
+                __nanosleep(1000);
             }
-            constexpr uint32_t kPerThread = kChunk / 4 / kConsumers;
-            float4 f[kPerThread];
-            if (len == kChunk) {  // every chunk but a row's last
-#pragma unroll
-                for (uint32_t jj = 0; jj < kPerThread; ++jj) f[jj] = r4[threadIdx.x + jj * kConsumers];
-            } else {
-#pragma unroll
-                for (uint32_t jj = 0; jj < kPerThread; ++jj) {
-                    const uint32_t q = threadIdx.x + jj * kConsumers;
-                    f[jj] = (4 * q < len) ? r4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[s]);  // stage s released by this warp
-            ++consumed;
-            // x -> fl(x * scale) is non-decreasing for a finite scale > 0, so
-            // the largest scaled value of a group of logits is the scaled
-            // largest raw value: one max per logit decides whether this
-            // thread's slice holds a candidate at all, and one max per float4
-            // which of its float4s do (fmaxf skips NaN, which reads as -inf).
-            float m4[kPerThread];
-#pragma unroll
-            for (uint32_t jj = 0; jj < kPerThread; ++jj)
-                m4[jj] = fmaxf(fmaxf(f[jj].x, f[jj].y), fmaxf(f[jj].z, f[jj].w));
-            float cmr = m4[0];
-#pragma unroll
-            for (uint32_t jj = 1; jj < kPerThread; ++jj) cmr = fmaxf(cmr, m4[jj]);
-            const float cm = __fmul_rn(cmr, scale);
-            lmax = fmaxf(lmax, cm);
-            if (cm >= tau) {
-#pragma unroll
-                for (uint32_t jj = 0; jj < kPerThread; ++jj) {
-                    if (__fmul_rn(m4[jj], scale) >= tau) {
-                        const float v[4] = {__fmul_rn(f[jj].x, scale), __fmul_rn(f[jj].y, scale),
-                                            __fmul_rn(f[jj].z, scale), __fmul_rn(f[jj].w, scale)};
-                        const uint32_t m = (v[0] >= tau ? 1u : 0u) | (v[1] >= tau ? 2u : 0u) |
-                                           (v[2] >= tau ? 4u : 0u) | (v[3] >= tau ? 8u : 0u);
-                        mark |= append_mask(L, count, ovf, m, v,
-                                            base_idx + 4 * (threadIdx.x + jj * kConsumers), kCompactAt);
-                    }
-                }
-            }
-            const bool last = c + 1 == c1;
-            // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
-            const uint32_t done = c + 1 - c0;
-            const bool refresh = last || (done < 8 ? (done & (done - 1)) == 0 && done > 1 : done % 8 == 0);
-            if (!refresh) continue;
-            if (t_bound) post_warp_bound(sm, lmax, t_bound, cw, par);
-            // One barrier per refresh: settles the list, publishes
-            // the bounds, and raises the rare events (a failed wait, a long
-            // list).
-            const bool want_compact = mark && cp.topk_active && !last;
-            mark = false;
-            if (consumers_any(!got || want_compact)) {
-                if (consumers_any(!got)) {
-                    stop = true;
-                    break;
-                }
-                // Compaction: tau rises to the list's own k-th largest value.
-                const uint32_t cnt = min(*count, kCap);
-                if (cnt >= cp.top_k) {
-                    const uint32_t kth = group_select_kth_largest<kConsumers, ConsumerSync>(
-                        cnt, cp.top_k, [&](uint32_t i) { return L.key[i]; }, sm.chist, sm.csel);
-                    tau = fmaxf(tau, key_to_float(kth));
-                    constexpr int kPer = kCap / kConsumers;
-                    uint32_t kk[kPer], ii[kPer];
-#pragma unroll
-                    for (int e = 0; e < kPer; ++e) {
-                        const uint32_t i = threadIdx.x + e * kConsumers;
-                        kk[e] = i < cnt ? L.key[i] : 0u;
-                        ii[e] = i < cnt ? L.idx[i] : 0u;
-                    }
-                    ConsumerSync::sync();
-                    if (threadIdx.x == 0) *count = 0;
-                    ConsumerSync::sync();
-#pragma unroll
-                    for (int e = 0; e < kPer; ++e) {
-                        const uint32_t i = threadIdx.x + e * kConsumers;
-                        append_candidate(L, count, ovf, i < cnt && key_to_float(kk[e]) >= tau, kk[e],
-                                         ii[e], kCap);
-                    }
-                    ConsumerSync::sync();
-                    if (*count > kCompactAt && threadIdx.x == 0) *ovf = 1;
-                }
-            }
-            if (t_bound) {
-                tau = fmaxf(tau, read_bound(sm, par));
-                par ^= 1u;
-            }
+            __threadfence();
+            sm.slot = got;
         }
-        if (stop) break;
-        if (kRecord) {
-            const float wm = warp_max(lmax);
-            if (lane == 0) sm.st_max[b][cw] = wm;
+        __syncthreads();
+        const uint32_t slot = sm.slot;
+        for (uint32_t k = 0; k < sm.ovf_count; ++k) {
+            const size_t row = sm.ovf_rows[k];
+            if (slot == ~0u) {
+                if (threadIdx.x == 0) {
+                    out_ids[row] = 0;
+                    out_status[row] = RSC_ROW_INTERNAL;
+                }
+                continue;
+            }
+            epilogue_row(cp, logits + row * row_stride, vocab, row,
+                         scratch + static_cast<size_t>(slot) * 4u * vocab, out_ids, out_status,
+                         out_probs, ls);
         }
-        if (threadIdx.x == 0) sm.tau_final[b] = tau;
-        ConsumerSync::sync();  // the row's list is complete
-        if (threadIdx.x == 0) mbar_arrive(&sm.list_full[b]);
+        __syncthreads();
+        if (threadIdx.x == 0 && slot != ~0u) {
+            __threadfence();
+            atomicExch(&slot_lock[slot], 0u);
+        }
     }
-    // A consumer that left early does not wait for the others: the finisher's
-    // and producer's bounded waits end the CTA.
 }
 
 // Vocab-sharded merge: each warp gathers the shards' records of one row into
@@ -1201,17 +1282,28 @@ StreamPlan stream_plan(size_t rows, uint32_t vocab, bool topk_active, uint32_t t
 
 cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                size_t row_stride, const CallParams &p, uint32_t *out_ids,
-                               int32_t *out_status, float *out_probs, uint32_t *large_rows,
-                               uint32_t *large_count, const StreamPlan &plan, void *seg_records,
-                               uint32_t *row_arrivals, cudaStream_t stream) {
+                               int32_t *out_status, float *out_probs, const StreamPlan &plan,
+                               void *seg_records, uint32_t *row_arrivals, uint32_t *scratch,
+                               uint32_t slots, uint32_t *slot_lock, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
     cudaError_t e = prepare(stream_topk_kernel<false>, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
-    stream_topk_kernel<false><<<plan.grid, kThreads, sizeof(StreamSmem), stream>>>(
-        logits, rows, vocab, row_stride, p, out_ids, out_status, out_probs, large_rows,
-        large_count, 0u, nullptr, split_record_bytes(plan.max_parts), plan.nch, plan.streamk,
-        plan.max_parts, static_cast<unsigned char *>(seg_records), row_arrivals);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = sizeof(StreamSmem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, stream_topk_kernel<false>, logits, rows, vocab, row_stride, p,
+                              out_ids, out_status, out_probs, scratch, slots, slot_lock, 0u,
+                              static_cast<unsigned char *>(nullptr),
+                              split_record_bytes(plan.max_parts), plan.nch, plan.streamk,
+                              plan.max_parts, static_cast<unsigned char *>(seg_records),
+                              row_arrivals);
 }
 
 cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shard_vocab,
@@ -1225,7 +1317,7 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
     const size_t grid = rows < ctas ? rows : ctas;
     const uint32_t nch = shard_vocab ? (shard_vocab + kChunk - 1) / kChunk : 1u;
     stream_topk_kernel<true><<<static_cast<unsigned>(grid), kThreads, sizeof(StreamSmem), stream>>>(
-        logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, nullptr,
+        logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, 0u, nullptr,
         shard_offset, static_cast<unsigned char *>(records), rec_bytes, nch, 0u, 1u, nullptr,
         nullptr);
     return cudaGetLastError();
