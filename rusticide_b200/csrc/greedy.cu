@@ -44,6 +44,9 @@ greedy_kernel(const float *__restrict__ logits, uint32_t vocab, size_t row_strid
     const uint32_t part = blockIdx.x;
     const size_t row = blockIdx.y;
     const float *p = logits + row * row_stride;
+    // The next launch on the stream may start as this grid's CTAs retire; it
+    // writes nothing before this grid completes (griddepcontrol.wait below).
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;");
 
     // Segment [lo, hi) of this CTA, cut at multiples of 4 elements.
     uint32_t seg = (vocab + parts - 1) / parts;
@@ -64,7 +67,7 @@ greedy_kernel(const float *__restrict__ logits, uint32_t vocab, size_t row_strid
     for (uint32_t i = body_hi + threadIdx.x; i < hi; i += blockDim.x) greedy_visit(__ldg(p + i), i, best, finite);
 
     const float4 *v4 = reinterpret_cast<const float4 *>(p + body_lo);
-    constexpr int kUnroll = 4;
+    constexpr int kUnroll = 8;
     uint32_t j = threadIdx.x;
     for (; j + (kUnroll - 1) * kGreedyThreads < nvec; j += kUnroll * kGreedyThreads) {
         float4 f[kUnroll];
@@ -108,6 +111,7 @@ greedy_kernel(const float *__restrict__ logits, uint32_t vocab, size_t row_strid
         unsigned long long b = warp_max(w.best);
         unsigned int f = __reduce_or_sync(0xffffffffu, w.any_finite);
         if (threadIdx.x == 0) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             if (vocab == 0 || !f) {
                 out_ids[row] = 0;
                 out_status[row] = RSC_ROW_NO_VALID_TOKENS;
@@ -138,13 +142,16 @@ cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size
     cfg.blockDim = dim3(kGreedyThreads, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = parts;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // Programmatic dependent launch: overlaps the previous launch's tail.
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, greedy_kernel, logits, vocab, row_stride, parts, out_ids,
                               out_status);
 }

@@ -594,27 +594,40 @@ __device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t
         // A +0.0 threshold also keeps -0.0 (IEEE -0.0 < +0.0 is false).
         floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
     }
-    const uint32_t n = gather_survivors(fw, ckey, cidx, count,
-                                        [&](uint32_t key, uint32_t idx, unsigned long long *it) {
-                                            *it = pack_key_index(~key, idx);
-                                            return key >= floor_key;
-                                        });
-    const uint32_t n64 = pow2_at_least(n);
-    for (uint32_t i = n + lane; i < n64; i += 32) fw.items[i] = ~0ull;
-    group_bitonic_sort<32, SyncWarp>(fw.items, n64);
-    const uint32_t nc = min(n, cap_entries);
-    for (uint32_t i = lane; i < nc; i += 32) {
-        const unsigned long long x = fw.items[i];
-        rkey[i] = ~static_cast<uint32_t>(x >> 32);
-        ridx[i] = static_cast<uint32_t>(x);
+    // The entries above the floor (fewer than k of them), then entries at the
+    // floor while room remains: whatever is dropped is tied with last_key,
+    // the smallest key kept. No order is needed: the merge reads the set.
+    uint32_t n_above = 0, n_at = 0, nc = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        for (uint32_t base = 0; base < count; base += 32) {
+            const uint32_t i = base + lane;
+            uint32_t key = 0, idx = 0;
+            bool take = false;
+            if (i < count) {
+                key = ckey[i];
+                idx = cidx[i];
+                take = pass == 0 ? key > floor_key : key == floor_key;
+            }
+            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+            const uint32_t pos = nc + __popc(ballot & ((1u << lane) - 1u));
+            if (take && pos < cap_entries) {
+                rkey[pos] = key;
+                ridx[pos] = idx;
+            }
+            const uint32_t got = __popc(ballot);
+            if (pass == 0) n_above += got;
+            else n_at += got;
+            nc = min(nc + got, cap_entries);
+        }
     }
     if (lane == 0) {
+        const uint32_t n = n_above + n_at;
         h->max_scaled = M;
         h->sum_exp = S;
         h->n_finite = nfin;
         h->n_cand = nc;
         h->n_dropped = n - nc;
-        h->last_key = nc ? ~static_cast<uint32_t>(fw.items[nc - 1] >> 32) : 0u;
+        h->last_key = n_at ? floor_key : 0u;
         h->flags = 0;
         h->tau = key_to_float(floor_key);
     }
@@ -633,37 +646,47 @@ template <typename RecAt>
 __device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uint32_t n,
                                   uint32_t cap_entries, const CallParams &cp, bool *ok) {
     const int lane = threadIdx.x & 31;
-    bool good = true;
-    float tau = -3.402823466e38f;
-    bool any_dropped = false;
-    for (uint32_t s = 0; s < n; ++s) {
-        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(s));
-        if (__ldcg(h + 6)) good = false;
-        tau = fmaxf(tau, __uint_as_float(__ldcg(h + 7)));
-        any_dropped |= __ldcg(h + 4) > 0;
+    // Headers: lane s reads part s (n <= 32), all at once.
+    uint32_t flags = 0, ndrop = 0, ncand = 0;
+    float tau_s = -3.402823466e38f;
+    if (static_cast<uint32_t>(lane) < n) {
+        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(lane));
+        ncand = min(__ldcg(h + 3), cap_entries);
+        ndrop = __ldcg(h + 4);
+        flags = __ldcg(h + 6);
+        tau_s = __uint_as_float(__ldcg(h + 7));
     }
+    bool good = !__any_sync(0xffffffffu, flags != 0u);
+    float tau = tau_s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tau = fmaxf(tau, __shfl_xor_sync(0xffffffffu, tau, o));
+    const bool any_dropped = __any_sync(0xffffffffu, ndrop > 0u);
     uint32_t count = 0;
     for (uint32_t s = 0; s < n && good; ++s) {
-        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(s));
-        const uint32_t nc = min(__ldcg(h + 3), cap_entries);
-        const uint32_t *rkey = h + 8;
+        const uint32_t nc = __shfl_sync(0xffffffffu, ncand, static_cast<int>(s));
+        const uint32_t *rkey = reinterpret_cast<const uint32_t *>(rec_at(s)) + 8;
         const uint32_t *ridx = rkey + cap_entries;
-        for (uint32_t base = 0; base < nc; base += 32) {
-            const uint32_t i = base + lane;
-            uint32_t key = 0, idx = 0;
-            bool keep = false;
-            if (i < nc) {
-                key = __ldcg(rkey + i);
-                idx = __ldcg(ridx + i);
-                keep = key_to_float(key) >= tau;
+        constexpr int kBatchLoads = 4;  // loads in flight per lane
+        for (uint32_t base = 0; base < nc; base += 32 * kBatchLoads) {
+            uint32_t kk[kBatchLoads], ii[kBatchLoads];
+#pragma unroll
+            for (int q = 0; q < kBatchLoads; ++q) {
+                const uint32_t i = base + q * 32 + lane;
+                kk[q] = i < nc ? __ldcg(rkey + i) : 0u;
+                ii[q] = i < nc ? __ldcg(ridx + i) : 0u;
             }
-            const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
-            const uint32_t pos = count + __popc(ballot & ((1u << lane) - 1u));
-            if (keep && pos < kCap) {
-                L.key[pos] = key;
-                L.idx[pos] = idx;
+#pragma unroll
+            for (int q = 0; q < kBatchLoads; ++q) {
+                const uint32_t i = base + q * 32 + lane;
+                const bool keep = i < nc && key_to_float(kk[q]) >= tau;
+                const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+                const uint32_t pos = count + __popc(ballot & ((1u << lane) - 1u));
+                if (keep && pos < kCap) {
+                    L.key[pos] = kk[q];
+                    L.idx[pos] = ii[q];
+                }
+                count += __popc(ballot);
             }
-            count += __popc(ballot);
         }
     }
     if (count > kCap) good = false;
@@ -1329,9 +1352,7 @@ cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows
     if (rows == 0) return cudaSuccess;
     cudaError_t e = prepare(shard_merge_kernel, sizeof(MergeSmem));
     if (e != cudaSuccess) return e;
-    size_t grid = (rows + kMergeWarps - 1) / kMergeWarps;
-    const size_t cap = static_cast<size_t>(num_sms) * 2;
-    if (grid > cap) grid = cap;
+    const size_t grid = (rows + kMergeWarps - 1) / kMergeWarps;
     shard_merge_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem), stream>>>(
         static_cast<const unsigned char *>(records), n_shards, rows, rec_bytes, p, out_ids,
         out_status, out_probs);
