@@ -109,14 +109,8 @@ __device__ __forceinline__ void load_exp_table(double *dst) {
     if (threadIdx.x < 32) dst[threadIdx.x] = kExp2Table.t[threadIdx.x];
 }
 
-// `tab` points at the 32-entry table (shared memory in hot loops).
-__device__ __forceinline__ float expf_ref(float x, const double *tab) {
-    if (!(x >= -104.0f)) {            // -inf, below the subnormal range, or NaN
-        return (x != x) ? x : 0.0f;   // glibc: exp(NaN) = NaN, otherwise +0
-    }
-    if (x > 0.0f) {                   // not reached by the sampler (x = v - max)
-        if (x > 88.72283172607421875f) return kPosInf;
-    }
+// The method's core for x in [-104, 88.72...] (no range checks).
+__device__ __forceinline__ float expf_core(float x, const double *tab) {
     const double kInvLn2N = 0x1.71547652b82fep+0 * 32.0;
     const double kShift = 0x1.8p+52;
     const double c0 = 0x1.c6af84b912394p-5 / (32.0 * 32.0 * 32.0);
@@ -137,6 +131,15 @@ __device__ __forceinline__ float expf_ref(float x, const double *tab) {
     y = __fma_rn(z, r2, y);
     y = __dmul_rn(y, s);
     return __double2float_rn(y);
+}
+
+// `tab` points at the 32-entry table (shared memory in hot loops).
+__device__ __forceinline__ float expf_ref(float x, const double *tab) {
+    if (!(x >= -104.0f)) {            // -inf, below the subnormal range, or NaN
+        return (x != x) ? x : 0.0f;   // glibc: exp(NaN) = NaN, otherwise +0
+    }
+    if (x > 88.72283172607421875f) return kPosInf;
+    return expf_core(x, tab);
 }
 
 // ---------------------------------------------------------------------------
