@@ -267,6 +267,33 @@ RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t rows, size_t
                                       float *d_out_probs, void *stream);
 
 /*
+ * LM-head GEMM (no reference counterpart as one call: the reference computes
+ * the logits with a host matvec, crates/rusticide-transformer/src/
+ * decoder.rs:104-105, then samples them). d_hidden is rows x dim bf16
+ * (row-major), d_weight is vocab x dim bf16 (row-major, the nn.Linear
+ * layout); logits = hidden . weight^T with bf16 products accumulated in f32
+ * on the tensor cores. dim must be a multiple of 8 and both pointers 16-byte
+ * aligned.
+ *
+ * rsc_lmhead_logits writes the rows x vocab f32 logits (dense).
+ * rsc_lmhead_sample samples them without writing them: the same GEMM keeps
+ * each row's top-k candidates in its epilogue and a merge finishes every row;
+ * the result equals rsc_sample on the logits rsc_lmhead_logits returns, bit
+ * for bit. It requires top-k on with top_k <= 40 and a finite T > 0 (else
+ * RSC_ERR_INVALID_ARGUMENT); a row with more than 24 logits tied at its k-th
+ * value reports RSC_ROW_INTERNAL and is sampled with rsc_lmhead_logits +
+ * rsc_sample instead. The first call allocates the handle's LM-head records.
+ */
+RSC_API rsc_status rsc_lmhead_logits(rsc_sampler *sampler, const void *d_hidden,
+                                     const void *d_weight, size_t rows, size_t dim, size_t vocab,
+                                     float *d_logits, void *stream);
+RSC_API rsc_status rsc_lmhead_sample(rsc_sampler *sampler, const void *d_hidden,
+                                     const void *d_weight, size_t rows, size_t dim, size_t vocab,
+                                     const rsc_params *params, const float *d_uniforms,
+                                     uint64_t *d_rng_states, uint32_t *d_out_ids,
+                                     int32_t *d_out_status, float *d_out_probs, void *stream);
+
+/*
  * Evaluates the library's binary32 exp, the function the sampler applies to
  * v - max (Rust's f32::exp, i.e. glibc expf, src/filters.rs:7 and
  * src/candidates.rs:64), on n device floats: d_y[i] = exp(d_x[i]). Exposed so

@@ -28,6 +28,8 @@ struct rsc_sampler {
     uint32_t plan_vocab = 0, plan_topk = 0;
     bool plan_valid = false;
     void *seg_records = nullptr;      // [max_units] records of split_record_bytes(splits >= 2)
+    void *lm_records = nullptr;       // [kLmheadMaxParts][max_rows] LM-head records (on first use)
+    uint32_t *lm_error = nullptr;     // timeout flag of the LM-head kernel
     uint32_t *row_arrivals = nullptr; // [max_rows], zero between calls
     // Device staging of rsc_pick_host.
     float *stage_logits = nullptr;
@@ -231,6 +233,8 @@ rsc_status rsc_sampler_destroy(rsc_sampler *s) {
     cudaFree(s->slot_lock);
     cudaFree(s->scratch);
     cudaFree(s->seg_records);
+    cudaFree(s->lm_records);
+    cudaFree(s->lm_error);
     cudaFree(s->row_arrivals);
     cudaFree(s->stage_logits);
     cudaFree(s->stage_uniforms);
@@ -426,6 +430,101 @@ rsc_status rsc_shard_merge(rsc_sampler *s, const void *d_records, size_t n_shard
                                             rsc::shard_record_bytes(params->top_k), cp, d_out_ids,
                                             d_out_status, d_out_probs, s->num_sms,
                                             static_cast<cudaStream_t>(stream));
+    ++s->launches;
+    return cuda_status(e);
+}
+
+namespace {
+
+rsc_status check_lmhead(const rsc_sampler *s, const void *d_hidden, const void *d_weight,
+                        size_t rows, size_t dim, size_t vocab) {
+    if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
+    if (vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (rows > s->max_rows) return RSC_ERR_CAPACITY;
+    if (rows > 0 && (vocab == 0 || dim == 0 || dim % 8 != 0)) return RSC_ERR_INVALID_SHAPE;
+    if (dim > (size_t{1} << 30)) return RSC_ERR_INVALID_SHAPE;
+    if (rows > 0 && (!d_hidden || !d_weight)) return RSC_ERR_INVALID_ARGUMENT;
+    if (((reinterpret_cast<uintptr_t>(d_hidden) | reinterpret_cast<uintptr_t>(d_weight)) & 15u) != 0)
+        return RSC_ERR_INVALID_ARGUMENT;
+    return RSC_OK;
+}
+
+// The LM-head records and the timeout flag, allocated on the first LM-head
+// call of the handle.
+rsc_status ensure_lm_records(rsc_sampler *s) {
+    if (s->lm_records) return RSC_OK;
+    // Part records, then the group records of the two-level merge.
+    const size_t bytes = static_cast<size_t>(rsc::kLmheadMaxParts + rsc::kLmheadMaxParts / 2) *
+                         s->max_rows * rsc::shard_record_bytes(rsc::kLmheadRowCap - RSC_SHARD_TIE_CAP);
+    if (cudaMalloc(&s->lm_records, bytes) != cudaSuccess) return RSC_ERR_CUDA;
+    if (cudaMalloc(&s->lm_error, sizeof(uint32_t)) != cudaSuccess) return RSC_ERR_CUDA;
+    if (cudaMemset(s->lm_error, 0, sizeof(uint32_t)) != cudaSuccess) return RSC_ERR_CUDA;
+    return RSC_OK;
+}
+
+}  // namespace
+
+rsc_status rsc_lmhead_logits(rsc_sampler *s, const void *d_hidden, const void *d_weight,
+                             size_t rows, size_t dim, size_t vocab, float *d_logits, void *stream) {
+    rsc_status st = check_lmhead(s, d_hidden, d_weight, rows, dim, vocab);
+    if (st != RSC_OK) return st;
+    if (rows == 0) return RSC_OK;
+    if (!d_logits) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    st = ensure_lm_records(s);
+    if (st != RSC_OK) return st;
+    const uint32_t v = static_cast<uint32_t>(vocab);
+    rsc_params prm{1.0f, 0, 1.0f, 1.0f, 0};
+    const rsc::CallParams cp = make_params(prm, vocab, nullptr, nullptr);
+    const uint32_t parts = rsc::lmhead_parts(rows, v, s->num_sms);
+    cudaError_t e = rsc::launch_lmhead(d_hidden, d_weight, rows, static_cast<uint32_t>(dim), v, cp,
+                                       d_logits, nullptr, 0, parts, s->lm_error,
+                                       static_cast<cudaStream_t>(stream));
+    ++s->launches;
+    return cuda_status(e);
+}
+
+rsc_status rsc_lmhead_sample(rsc_sampler *s, const void *d_hidden, const void *d_weight,
+                             size_t rows, size_t dim, size_t vocab, const rsc_params *params,
+                             const float *d_uniforms, uint64_t *d_rng_states, uint32_t *d_out_ids,
+                             int32_t *d_out_status, float *d_out_probs, void *stream) {
+    rsc_status st = check_lmhead(s, d_hidden, d_weight, rows, dim, vocab);
+    if (st != RSC_OK) return st;
+    if (!params) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows == 0) return RSC_OK;
+    if (!d_out_ids || !d_out_status) return RSC_ERR_INVALID_ARGUMENT;
+    const rsc::CallParams cp = make_params(*params, vocab, d_uniforms, d_rng_states);
+    if (!cp.topk_active || !cp.normal_scale ||
+        params->top_k + RSC_SHARD_TIE_CAP > rsc::kLmheadRowCap)
+        return RSC_ERR_INVALID_ARGUMENT;
+    if (!cp.argmax_branch && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    st = ensure_lm_records(s);
+    if (st != RSC_OK) return st;
+    const uint32_t v = static_cast<uint32_t>(vocab);
+    const uint32_t parts = rsc::lmhead_parts(rows, v, s->num_sms);
+    const size_t rec_bytes = rsc::shard_record_bytes(params->top_k);
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    cudaError_t e = rsc::launch_lmhead(d_hidden, d_weight, rows, static_cast<uint32_t>(dim), v, cp,
+                                       nullptr, s->lm_records, rec_bytes, parts, s->lm_error, strm);
+    ++s->launches;
+    if (e != cudaSuccess) return RSC_ERR_CUDA;
+    // One merge list holds the records of kSmallCap / (k + 24) parts; more
+    // parts are first reduced in groups of that many.
+    const uint32_t group = rsc::kSmallCap / (params->top_k + RSC_SHARD_TIE_CAP);
+    const void *final_records = s->lm_records;
+    size_t n_final = parts;
+    if (parts > group) {
+        unsigned char *groups = static_cast<unsigned char *>(s->lm_records) +
+                                static_cast<size_t>(parts) * rows * rec_bytes;
+        e = rsc::launch_shard_reduce(s->lm_records, parts, rows, rec_bytes, group, cp, groups, strm);
+        ++s->launches;
+        if (e != cudaSuccess) return RSC_ERR_CUDA;
+        final_records = groups;
+        n_final = (parts + group - 1) / group;
+    }
+    e = rsc::launch_shard_merge(final_records, n_final, rows, rec_bytes, cp, d_out_ids, d_out_status,
+                                d_out_probs, s->num_sms, strm);
     ++s->launches;
     return cuda_status(e);
 }

@@ -70,6 +70,19 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, uint32_t *scratch, uint32_t slots, cudaStream_t stream);
 
+// LM-head GEMM with the sampler fused into its epilogue (lmhead.cu). A row
+// keeps at most kLmheadRowCap candidates per part, so top_k <= kLmheadRowCap -
+// RSC_SHARD_TIE_CAP; a row is spread over at most kLmheadMaxParts parts.
+constexpr uint32_t kLmheadRowCap = 64;
+constexpr uint32_t kLmheadMaxParts = 32;
+uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms);
+// logits != nullptr: writes rows x vocab f32 logits; otherwise writes one
+// shard record per (part, row) into records ([parts][rows], rec_bytes each).
+cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, uint32_t dim,
+                          uint32_t vocab, const CallParams &p, float *logits, void *records,
+                          size_t rec_bytes, uint32_t parts, uint32_t *error_flag,
+                          cudaStream_t stream);
+
 // Vocab-sharded record: this header, then uint32 key[k + RSC_SHARD_TIE_CAP]
 // and uint32 index[k + RSC_SHARD_TIE_CAP] (global indices), entries sorted by
 // (key desc, index asc). Keys are f32::total_cmp keys of the scaled logits.
@@ -97,6 +110,11 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
                                  void *records, size_t rec_bytes, int num_sms,
                                  cudaStream_t stream);
 
+// Merges the part records [n_parts][rows] in groups of `group` (at most
+// kSmallCap / (k + RSC_SHARD_TIE_CAP) parts) into group records
+// [ceil(n_parts / group)][rows] of the same format.
+cudaError_t launch_shard_reduce(const void *records, size_t n_parts, size_t rows, size_t rec_bytes,
+                                uint32_t group, const CallParams &p, void *out, cudaStream_t stream);
 cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows, size_t rec_bytes,
                                const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                                float *out_probs, int num_sms, cudaStream_t stream);

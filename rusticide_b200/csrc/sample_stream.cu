@@ -117,10 +117,6 @@ __device__ __forceinline__ RowGeom row_geom(const float *logits, size_t row, siz
     return g;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
 // Barrier of the consumer warps that also ORs a predicate across them: every
 // consumer thread gets the same answer.
 __device__ __forceinline__ bool consumers_any(bool p) {
@@ -644,7 +640,8 @@ __device__ void record_list(FinishWork &fw, const uint32_t *ckey, const uint32_t
 // are read past L1 (ld.global.cg).
 template <typename RecAt>
 __device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uint32_t n,
-                                  uint32_t cap_entries, const CallParams &cp, bool *ok) {
+                                  uint32_t cap_entries, const CallParams &cp, bool *ok,
+                                  float *tau_out = nullptr) {
     const int lane = threadIdx.x & 31;
     // Headers: lane s reads part s (n <= 32), all at once.
     uint32_t flags = 0, ndrop = 0, ncand = 0;
@@ -660,6 +657,7 @@ __device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uin
     float tau = tau_s;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) tau = fmaxf(tau, __shfl_xor_sync(0xffffffffu, tau, o));
+    if (tau_out) *tau_out = tau;
     const bool any_dropped = __any_sync(0xffffffffu, ndrop > 0u);
     uint32_t count = 0;
     for (uint32_t s = 0; s < n && good; ++s) {
@@ -882,7 +880,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     // First chunk: lane maxima before filtering, so that tau is
                     // already high for this chunk's own logits.
                     float cmr = kNegInf;
-    #pragma unroll
+#pragma unroll
                     for (uint32_t jj = 0; jj < kChunk / 4 / kConsumers; ++jj) {
                         const uint32_t q = threadIdx.x + jj * kConsumers;
                         if (4 * q < len) {
@@ -898,14 +896,26 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     }
                     tau = fmaxf(tau, read_bound(sm, par));
                     par ^= 1u;
+                    if (len < kChunk && len >= cp.top_k) {
+                        // A partial first chunk (a row's tail part, or a short
+                        // row) spreads too thin over the lanes for their maxima
+                        // to bound the k-th largest value: take the chunk's own
+                        // exact k-th largest instead (the stage is still held).
+                        const float *ring = sm.ring[s];
+                        const uint32_t kth = group_select_kth_largest<kConsumers, ConsumerSync>(
+                            len, cp.top_k,
+                            [&](uint32_t i) { return total_key(scale_logit(ring[i], scale)); },
+                            sm.chist, sm.csel);
+                        tau = fmaxf(tau, key_to_float(kth));
+                    }
                 }
                 constexpr uint32_t kPerThread = kChunk / 4 / kConsumers;
                 float4 f[kPerThread];
                 if (len == kChunk) {  // every chunk but a row's last
-    #pragma unroll
+#pragma unroll
                     for (uint32_t jj = 0; jj < kPerThread; ++jj) f[jj] = r4[threadIdx.x + jj * kConsumers];
                 } else {
-    #pragma unroll
+#pragma unroll
                     for (uint32_t jj = 0; jj < kPerThread; ++jj) {
                         const uint32_t q = threadIdx.x + jj * kConsumers;
                         f[jj] = (4 * q < len) ? r4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
@@ -920,16 +930,16 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 // thread's slice holds a candidate at all, and one max per float4
                 // which of its float4s do (fmaxf skips NaN, which reads as -inf).
                 float m4[kPerThread];
-    #pragma unroll
+#pragma unroll
                 for (uint32_t jj = 0; jj < kPerThread; ++jj)
                     m4[jj] = fmaxf(fmaxf(f[jj].x, f[jj].y), fmaxf(f[jj].z, f[jj].w));
                 float cmr = m4[0];
-    #pragma unroll
+#pragma unroll
                 for (uint32_t jj = 1; jj < kPerThread; ++jj) cmr = fmaxf(cmr, m4[jj]);
                 const float cm = __fmul_rn(cmr, scale);
                 lmax = fmaxf(lmax, cm);
                 if (cm >= tau) {
-    #pragma unroll
+#pragma unroll
                     for (uint32_t jj = 0; jj < kPerThread; ++jj) {
                         if (__fmul_rn(m4[jj], scale) >= tau) {
                             const float v[4] = {__fmul_rn(f[jj].x, scale), __fmul_rn(f[jj].y, scale),
@@ -965,7 +975,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                         tau = fmaxf(tau, key_to_float(kth));
                         constexpr int kPer = kCap / kConsumers;
                         uint32_t kk[kPer], ii[kPer];
-    #pragma unroll
+#pragma unroll
                         for (int e = 0; e < kPer; ++e) {
                             const uint32_t i = threadIdx.x + e * kConsumers;
                             kk[e] = i < cnt ? L.key[i] : 0u;
@@ -974,7 +984,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                         ConsumerSync::sync();
                         if (threadIdx.x == 0) *count = 0;
                         ConsumerSync::sync();
-    #pragma unroll
+#pragma unroll
                         for (int e = 0; e < kPer; ++e) {
                             const uint32_t i = threadIdx.x + e * kConsumers;
                             append_candidate(L, count, ovf, i < cnt && key_to_float(kk[e]) >= tau, kk[e],
@@ -1228,6 +1238,46 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
     }
 }
 
+// Two-level merge for rows spread over more parts than one candidate list can
+// take: each warp merges up to kReduceGroup part records of one row into one
+// record of the same format (the group's candidates at or above the largest
+// of its parts' bounds, capped at k + RSC_SHARD_TIE_CAP like a part record).
+__global__ void __launch_bounds__(kMergeWarps * 32)
+shard_reduce_kernel(const unsigned char *__restrict__ records, size_t n_parts, size_t rows,
+                    size_t rec_bytes, uint32_t group, CallParams cp,
+                    unsigned char *__restrict__ out) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    MergeSmem &sm = *reinterpret_cast<MergeSmem *>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    CandList &L = sm.list[warp];
+    FinishWork &fw = sm.fw[warp];
+    const size_t n_groups = (n_parts + group - 1) / group;
+    const uint32_t cap = cp.top_k + RSC_SHARD_TIE_CAP;
+    for (size_t w = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; w < n_groups * rows;
+         w += static_cast<size_t>(gridDim.x) * kMergeWarps) {
+        const size_t g = w / rows, row = w % rows;
+        const size_t p0 = g * group;
+        const uint32_t n = static_cast<uint32_t>(min(static_cast<size_t>(group), n_parts - p0));
+        bool ok = true;
+        float tau = 0.0f;
+        const uint32_t count = merge_records(
+            L, fw, [&](uint32_t part) { return records + ((p0 + part) * rows + row) * rec_bytes; },
+            n, cap, cp, &ok, &tau);
+        unsigned char *rec = out + (g * rows + row) * rec_bytes;
+        if (!ok) {
+            if (lane == 0) {
+                ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                h->n_cand = 0;
+                h->n_dropped = 0;
+                h->flags = 1;
+            }
+            __syncwarp();
+            continue;
+        }
+        record_list(fw, L.key, L.idx, count, cp, 0.0f, 0.0f, 0u, rec, cap, tau);
+    }
+}
+
 template <typename K>
 cudaError_t prepare(K kernel, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1343,6 +1393,19 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
         logits, rows, shard_vocab, row_stride, p, nullptr, nullptr, nullptr, nullptr, 0u, nullptr,
         shard_offset, static_cast<unsigned char *>(records), rec_bytes, nch, 0u, 1u, nullptr,
         nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shard_reduce(const void *records, size_t n_parts, size_t rows, size_t rec_bytes,
+                                uint32_t group, const CallParams &p, void *out, cudaStream_t stream) {
+    if (rows == 0 || n_parts == 0) return cudaSuccess;
+    cudaError_t e = prepare(shard_reduce_kernel, sizeof(MergeSmem));
+    if (e != cudaSuccess) return e;
+    const size_t n_groups = (n_parts + group - 1) / group;
+    const size_t grid = (n_groups * rows + kMergeWarps - 1) / kMergeWarps;
+    shard_reduce_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem), stream>>>(
+        static_cast<const unsigned char *>(records), n_parts, rows, rec_bytes, group, p,
+        static_cast<unsigned char *>(out));
     return cudaGetLastError();
 }
 

@@ -320,6 +320,44 @@ class Engine:
                                        _ptr(probs), _stream_ptr(self.device)), "rsc_shard_merge")
         return ids, status, probs
 
+    # -- LM head with the sampler fused into its epilogue ----------------------
+    @staticmethod
+    def _lmhead_args(hidden: torch.Tensor, weight: torch.Tensor):
+        if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+            raise TensorError("bf16", f"{hidden.dtype}/{weight.dtype}")
+        if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+            raise InvalidShape(list(hidden.shape) + list(weight.shape))
+        return hidden.contiguous(), weight.contiguous()
+
+    def lmhead_logits(self, hidden: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        """hidden . weight^T in f32 (bf16 inputs) on the tensor cores."""
+        hidden, weight = self._lmhead_args(hidden, weight)
+        rows, dim = hidden.shape
+        vocab = weight.shape[0]
+        self.ensure(rows, 1)
+        out = torch.empty((rows, vocab), dtype=torch.float32, device=self.device)
+        check(self.lib.rsc_lmhead_logits(self._h, hidden.data_ptr(), weight.data_ptr(), rows, dim,
+                                         vocab, out.data_ptr(), _stream_ptr(self.device)),
+              "rsc_lmhead_logits")
+        return out
+
+    def lmhead_sample(self, hidden: torch.Tensor, weight: torch.Tensor, params: SamplingParams,
+                      uniforms: Optional[torch.Tensor] = None,
+                      rng_states: Optional[torch.Tensor] = None, want_probs: bool = True,
+                      out=None):
+        """sample(hidden . weight^T) without writing the logits."""
+        hidden, weight = self._lmhead_args(hidden, weight)
+        rows, dim = hidden.shape
+        vocab = weight.shape[0]
+        self.ensure(rows, 1)
+        ids, status, probs = out if out is not None else self._outputs(rows, want_probs)
+        c = params.to_c()
+        check(self.lib.rsc_lmhead_sample(self._h, hidden.data_ptr(), weight.data_ptr(), rows, dim,
+                                         vocab, ctypes.byref(c), _ptr(uniforms), _ptr(rng_states),
+                                         ids.data_ptr(), status.data_ptr(), _ptr(probs),
+                                         _stream_ptr(self.device)), "rsc_lmhead_sample")
+        return ids, status, probs
+
 
 _ENGINES: dict[int, Engine] = {}
 

@@ -1,0 +1,86 @@
+"""LM-head GEMM with the sampler fused into its epilogue (rsc_lmhead_*).
+
+1. rsc_lmhead_logits against an f32 reference of the same product: bf16 x
+   bf16 products are exact in f32, so the only difference is the order of the
+   f32 sums, bounded by 2 * dim * 2^-24 * (|H| . |W|^T) per entry.
+2. rsc_lmhead_sample against rsc_sample on the logits rsc_lmhead_logits
+   returns: ids, statuses and probability bits identical (the fused epilogue
+   sees the same f32 values), and those rows match the oracle
+   (crates/rusticide-sampling/src/sampler.rs:44-54).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from rusticide_b200 import SamplingParams, engine
+from rusticide_b200.sampler import SamplingError
+
+pytestmark = pytest.mark.gpu
+
+# (rows, dim, vocab): partial row tiles, a dim that is not a multiple of 64,
+# partial vocab tiles, and a Qwen-sized vocab shard.
+SHAPES = [(1, 64, 300), (5, 256, 4096), (130, 1000, 5000), (64, 512, 18992)]
+
+
+def _inputs(rows, dim, vocab, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    h = torch.randn(rows, dim, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(vocab, dim, device="cuda", generator=g) * (3.0 / dim ** 0.5)).bfloat16()
+    # A few boosted vocabulary rows give peaked rows, as an LM head does.
+    hot = torch.randint(0, vocab, (8,), device="cuda", generator=g)
+    w[hot] = (w[hot].float() * 4.0).bfloat16()
+    return h, w
+
+
+@pytest.fixture(scope="module")
+def eng():
+    return engine(0)
+
+
+@pytest.mark.parametrize("rows,dim,vocab", SHAPES)
+def test_lmhead_logits_match_f32_product(eng, rows, dim, vocab):
+    h, w = _inputs(rows, dim, vocab, seed=rows * 131 + dim)
+    got = eng.lmhead_logits(h, w)
+    torch.cuda.synchronize()
+    hf, wf = h.float(), w.float()
+    want = hf @ wf.T
+    bound = 2.0 * dim * 2.0 ** -24 * (hf.abs() @ wf.abs().T) + 1e-30
+    err = (got - want).abs()
+    assert torch.isfinite(got).all()
+    assert (err <= bound).all(), f"max err {err.max().item()} vs bound {bound.max().item()}"
+
+
+@pytest.mark.parametrize("rows,dim,vocab", SHAPES)
+@pytest.mark.parametrize("temperature,top_k,top_p", [(0.8, 40, 0.95), (0.3, 40, 0.9),
+                                                     (1.0, 1, 1.0), (1.5, 8, 1.0)])
+def test_lmhead_sample_matches_sample_on_its_logits(eng, rows, dim, vocab, temperature, top_k,
+                                                    top_p):
+    h, w = _inputs(rows, dim, vocab, seed=rows * 17 + dim + vocab)
+    params = SamplingParams(temperature, top_k, top_p)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    u = torch.rand(rows, device="cuda", generator=g)
+    ids_f, st_f, pr_f = eng.lmhead_sample(h, w, params, uniforms=u)
+    logits = eng.lmhead_logits(h, w)
+    ids_s, st_s, pr_s = eng.sample(logits, params, uniforms=u)
+    torch.cuda.synchronize()
+    assert torch.equal(st_f, st_s)
+    assert torch.equal(ids_f, ids_s)
+    assert torch.equal(pr_f.view(torch.int32), pr_s.view(torch.int32))
+    assert (st_f & 0xFF).eq(0).all()
+
+    from oracle import oracle as O
+    x = logits.cpu().numpy()
+    ref = O.sample_rows(x, O.params(temperature, top_k, top_p), u.cpu().numpy(), threads=4)
+    assert np.array_equal(ids_f.cpu().numpy().astype(np.int64), ref["token"].astype(np.int64))
+
+
+def test_lmhead_rejects_unsupported_params(eng):
+    h, w = _inputs(2, 64, 300, seed=1)
+    u = torch.rand(2, device="cuda")
+    for params in (SamplingParams(0.8, 0, 0.95), SamplingParams(0.8, 100, 0.95),
+                   SamplingParams(float("inf"), 40, 0.95)):
+        with pytest.raises(Exception):
+            eng.lmhead_sample(h, w, params, uniforms=u)
+    with pytest.raises(SamplingError):
+        eng.lmhead_logits(h.float(), w)
