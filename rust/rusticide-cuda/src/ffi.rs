@@ -190,6 +190,31 @@ unsafe extern "C" {
         d_out_probs: *mut f32,
         stream: *mut c_void,
     ) -> c_int;
+    pub(crate) fn rsc_lmhead_logits(
+        sampler: *mut RscSampler,
+        d_hidden: *const c_void,
+        d_weight: *const c_void,
+        rows: usize,
+        dim: usize,
+        vocab: usize,
+        d_logits: *mut f32,
+        stream: *mut c_void,
+    ) -> c_int;
+    pub(crate) fn rsc_lmhead_sample(
+        sampler: *mut RscSampler,
+        d_hidden: *const c_void,
+        d_weight: *const c_void,
+        rows: usize,
+        dim: usize,
+        vocab: usize,
+        params: *const RscParams,
+        d_uniforms: *const f32,
+        d_rng_states: *mut u64,
+        d_out_ids: *mut u32,
+        d_out_status: *mut i32,
+        d_out_probs: *mut f32,
+        stream: *mut c_void,
+    ) -> c_int;
     pub(crate) fn rsc_expf(d_x: *const f32, d_y: *mut f32, n: usize, stream: *mut c_void) -> c_int;
     pub(crate) fn rsc_launch_count(sampler: *const RscSampler) -> u64;
 }

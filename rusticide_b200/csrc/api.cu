@@ -453,9 +453,9 @@ rsc_status check_lmhead(const rsc_sampler *s, const void *d_hidden, const void *
 // call of the handle.
 rsc_status ensure_lm_records(rsc_sampler *s) {
     if (s->lm_records) return RSC_OK;
-    // Part records, then the group records of the two-level merge.
-    const size_t bytes = static_cast<size_t>(rsc::kLmheadMaxParts + rsc::kLmheadMaxParts / 2) *
-                         s->max_rows * rsc::shard_record_bytes(rsc::kLmheadRowCap - RSC_SHARD_TIE_CAP);
+    // Part records, then the group records of each reduction level.
+    const size_t bytes = static_cast<size_t>(rsc::kLmheadRecordSlots) * s->max_rows *
+                         rsc::shard_record_bytes(rsc::kLmheadRowCap - RSC_SHARD_TIE_CAP);
     if (cudaMalloc(&s->lm_records, bytes) != cudaSuccess) return RSC_ERR_CUDA;
     if (cudaMalloc(&s->lm_error, sizeof(uint32_t)) != cudaSuccess) return RSC_ERR_CUDA;
     if (cudaMemset(s->lm_error, 0, sizeof(uint32_t)) != cudaSuccess) return RSC_ERR_CUDA;
@@ -510,21 +510,22 @@ rsc_status rsc_lmhead_sample(rsc_sampler *s, const void *d_hidden, const void *d
     ++s->launches;
     if (e != cudaSuccess) return RSC_ERR_CUDA;
     // One merge list holds the records of kSmallCap / (k + 24) parts; more
-    // parts are first reduced in groups of that many.
+    // parts are first reduced, level by level, in groups of that many.
     const uint32_t group = rsc::kSmallCap / (params->top_k + RSC_SHARD_TIE_CAP);
-    const void *final_records = s->lm_records;
-    size_t n_final = parts;
-    if (parts > group) {
-        unsigned char *groups = static_cast<unsigned char *>(s->lm_records) +
-                                static_cast<size_t>(parts) * rows * rec_bytes;
-        e = rsc::launch_shard_reduce(s->lm_records, parts, rows, rec_bytes, group, cp, groups, strm);
+    const unsigned char *cur = static_cast<const unsigned char *>(s->lm_records);
+    unsigned char *next = static_cast<unsigned char *>(s->lm_records) +
+                          static_cast<size_t>(parts) * rows * rec_bytes;
+    size_t n = parts;
+    while (n > group) {
+        e = rsc::launch_shard_reduce(cur, n, rows, rec_bytes, group, cp, next, strm);
         ++s->launches;
         if (e != cudaSuccess) return RSC_ERR_CUDA;
-        final_records = groups;
-        n_final = (parts + group - 1) / group;
+        n = (n + group - 1) / group;
+        cur = next;
+        next += n * rows * rec_bytes;
     }
-    e = rsc::launch_shard_merge(final_records, n_final, rows, rec_bytes, cp, d_out_ids, d_out_status,
-                                d_out_probs, s->num_sms, strm);
+    e = rsc::launch_shard_merge(cur, n, rows, rec_bytes, cp, d_out_ids, d_out_status, d_out_probs,
+                                s->num_sms, strm);
     ++s->launches;
     return cuda_status(e);
 }

@@ -38,14 +38,19 @@ constexpr int kUK = 16;         // k per tcgen05.mma (kind::f16)
 constexpr int kGStages = 3;
 constexpr int kGThreads = 192;
 constexpr int kEpiWarp0 = 2;
-constexpr int kRowCap = kLmheadRowCap;  // candidates a row keeps in shared memory
+constexpr uint32_t kRowCap = kLmheadRowCap;  // candidates a row keeps in shared memory
+constexpr uint32_t kChunkCols = 16;          // accumulator columns per epilogue step
 constexpr uint32_t kTmemCols = 2 * kBN;
 
 struct LmSmem {
     __nv_bfloat16 a[kGStages][kBM * kBK];  // 16 KiB per stage
     __nv_bfloat16 b[kGStages][kBN * kBK];  // 32 KiB per stage
-    uint32_t ckey[kRowCap][kBM];           // per-row candidate lists, row fastest
-    uint32_t cidx[kRowCap][kBM];
+    uint32_t ckey[kBM][kRowCap];           // per-row candidate lists
+    uint32_t cidx[kBM][kRowCap];
+    float tb[kBM / 32][kChunkCols][33];    // per-warp transpose of a 32-row chunk
+    float rtau[kBM];                       // per-row bound, candidate count, overflow
+    uint32_t rcount[kBM];
+    uint32_t rflag[kBM];
     uint64_t full[kGStages];
     uint64_t empty[kGStages];
     uint64_t acc_full[2];
@@ -100,6 +105,18 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// 16 consecutive accumulator columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // 32 consecutive accumulator columns of this thread's lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -115,31 +132,47 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// The k-th largest key among a row's n list entries (n >= k), by a bitwise
-// search over the key space (one thread).
-__device__ uint32_t row_kth_key(const LmSmem &sm, uint32_t r, uint32_t n, uint32_t k) {
+// One warp: the k-th largest key over a row's n list entries (n <= 64) and
+// one extra key per lane (where has_extra), by a bitwise search.
+__device__ __forceinline__ uint32_t warp_kth_key(const uint32_t *lkey, uint32_t n, uint32_t extra,
+                                                 bool has_extra, uint32_t k) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool va = lane < n, vb = lane + 32u < n;
+    const uint32_t a = va ? lkey[lane] : 0u, b = vb ? lkey[lane + 32u] : 0u;
     uint32_t res = 0;
     for (int bit = 31; bit >= 0; --bit) {
         const uint32_t cand = res | (1u << bit);
-        uint32_t c = 0;
-        for (uint32_t i = 0; i < n; ++i) c += sm.ckey[i][r] >= cand ? 1u : 0u;
-        if (c >= k) res = cand;
+        const uint32_t c = (va && a >= cand ? 1u : 0u) + (vb && b >= cand ? 1u : 0u) +
+                           (has_extra && extra >= cand ? 1u : 0u);
+        if (__reduce_add_sync(0xffffffffu, c) >= k) res = cand;
     }
     return res;
 }
 
-// Keeps a row's entries at or above floor_key; returns their number.
-__device__ uint32_t row_compact(LmSmem &sm, uint32_t r, uint32_t n, uint32_t floor_key) {
-    uint32_t m = 0;
-    for (uint32_t i = 0; i < n; ++i) {
-        const uint32_t key = sm.ckey[i][r];
-        if (key >= floor_key) {
-            sm.ckey[m][r] = key;
-            sm.cidx[m][r] = sm.cidx[i][r];
-            ++m;
-        }
+// One warp: keeps a row's list entries at or above floor_key, in place;
+// returns their number.
+__device__ __forceinline__ uint32_t warp_compact(uint32_t *lkey, uint32_t *lidx, uint32_t n,
+                                                 uint32_t floor_key) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool va = lane < n, vb = lane + 32u < n;
+    const uint32_t ka = va ? lkey[lane] : 0u, kb = vb ? lkey[lane + 32u] : 0u;
+    const uint32_t ia = va ? lidx[lane] : 0u, ib = vb ? lidx[lane + 32u] : 0u;
+    const bool keep_a = va && ka >= floor_key, keep_b = vb && kb >= floor_key;
+    const uint32_t ba = __ballot_sync(0xffffffffu, keep_a), bb = __ballot_sync(0xffffffffu, keep_b);
+    const uint32_t lt = (1u << lane) - 1u;
+    __syncwarp();
+    if (keep_a) {
+        const uint32_t pos = __popc(ba & lt);
+        lkey[pos] = ka;
+        lidx[pos] = ia;
     }
-    return m;
+    if (keep_b) {
+        const uint32_t pos = __popc(ba) + __popc(bb & lt);
+        lkey[pos] = kb;
+        lidx[pos] = ib;
+    }
+    __syncwarp();
+    return __popc(ba) + __popc(bb);
 }
 
 template <bool kFused>
@@ -252,11 +285,13 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
         const uint32_t r = lane_base + lane;
         const uint32_t grow = m0 + r;
         const float scale = cp.scale;
-        uint32_t count = 0;
-        float tau = -3.402823466e38f;
-        float vmax = kNegInf;
-        bool overflow = false;
+        float vmax = kNegInf;  // this thread's row maximum
         const uint32_t k = cp.top_k;
+        // Row state: no candidates, the bound that admits everything but -inf.
+        sm.rcount[r] = 0;
+        sm.rtau[r] = -3.402823466e38f;
+        sm.rflag[r] = 0;
+        __syncwarp();
         for (uint32_t t = t0, j = 0; t < t1; ++t, ++j) {
             const uint32_t buf = j & 1u;
             bool got = mbar_wait(&sm.acc_full[buf], (j >> 1) & 1u);
@@ -265,41 +300,109 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
                 break;
             }
             tc_fence_after();
-            for (uint32_t c = 0; c < kBN; c += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + buf * kBN + c + (lane_base << 16), v);
-                const uint32_t col0 = t * kBN + c;
-                if (!kFused) {
+            if (!kFused) {
+                for (uint32_t c = 0; c < kBN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + buf * kBN + c + (lane_base << 16), v);
+                    const uint32_t col0 = t * kBN + c;
                     if (grow < rows) {
 #pragma unroll
                         for (int q = 0; q < 32; ++q)
                             if (col0 + q < vocab)
                                 logits[static_cast<size_t>(grow) * vocab + col0 + q] = __uint_as_float(v[q]);
                     }
-                    continue;
                 }
-                if (grow >= rows || overflow) continue;
+            } else {
+                const uint32_t w = static_cast<uint32_t>(warp) & 3u;
+                if (j == 0) {
+                    // First tile of the part: a starting bound for each row.
+                    // Its 256 columns fall into 48 disjoint groups (column
+                    // within a 16-column step, step mod 3); the smallest of the
+                    // 48 group maxima has 48 distinct values at or above it, so
+                    // it is at most the part's k-th largest value (k <= 48).
+                    float gm[3][kChunkCols];
 #pragma unroll
-                for (int q = 0; q < 32; ++q) {
-                    const float x = scale_logit(__uint_as_float(v[q]), scale);
-                    const bool in = col0 + q < vocab;
-                    vmax = in ? fmaxf(vmax, x) : vmax;
-                    if (in && x >= tau) {
-                        if (count == static_cast<uint32_t>(kRowCap)) {
-                            // Full: tau rises to the list's k-th largest value.
-                            uint32_t kth = row_kth_key(sm, r, count, k);
-                            const uint32_t floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
-                            tau = key_to_float(floor_key);
-                            count = row_compact(sm, r, count, floor_key);
-                            if (count == static_cast<uint32_t>(kRowCap)) {
-                                overflow = true;  // more than kRowCap - k ties
-                                break;
-                            }
-                            if (!(x >= tau)) continue;
+                    for (int g = 0; g < 3; ++g)
+#pragma unroll
+                        for (int q = 0; q < static_cast<int>(kChunkCols); ++q) gm[g][q] = kNegInf;
+                    for (uint32_t c = 0, step = 0; c < kBN; c += kChunkCols, ++step) {
+                        uint32_t v[kChunkCols];
+                        tmem_ld16(tmem + buf * kBN + c + (lane_base << 16), v);
+                        const uint32_t col0 = t * kBN + c;
+                        const uint32_t g = step % 3u;
+#pragma unroll
+                        for (int q = 0; q < static_cast<int>(kChunkCols); ++q) {
+                            const float x = col0 + q < vocab ? scale_logit(__uint_as_float(v[q]), scale)
+                                                             : kNegInf;
+                            if (g == 0) gm[0][q] = fmaxf(gm[0][q], x);
+                            else if (g == 1) gm[1][q] = fmaxf(gm[1][q], x);
+                            else gm[2][q] = fmaxf(gm[2][q], x);
                         }
-                        sm.ckey[count][r] = total_key(x);
-                        sm.cidx[count][r] = col0 + q;
-                        ++count;
+                    }
+                    float b = kPosInf;
+#pragma unroll
+                    for (int g = 0; g < 3; ++g)
+#pragma unroll
+                        for (int q = 0; q < static_cast<int>(kChunkCols); ++q) b = fminf(b, gm[g][q]);
+                    if (grow < rows && k <= 3u * kChunkCols && b > sm.rtau[r]) sm.rtau[r] = b;
+                    __syncwarp();
+                }
+                for (uint32_t c = 0; c < kBN; c += kChunkCols) {
+                    uint32_t v[kChunkCols];
+                    tmem_ld16(tmem + buf * kBN + c + (lane_base << 16), v);
+                    const uint32_t col0 = t * kBN + c;
+                    // Thread = row: scale, track the row maximum, and transpose
+                    // the 32 x 16 block through shared memory.
+#pragma unroll
+                    for (int q = 0; q < static_cast<int>(kChunkCols); ++q) {
+                        const float x = scale_logit(__uint_as_float(v[q]), scale);
+                        if (col0 + q < vocab) vmax = fmaxf(vmax, x);
+                        sm.tb[w][q][lane] = x;
+                    }
+                    __syncwarp();
+                    // Warp = row: the 16 values of each of the warp's rows in
+                    // turn, filtered by the row's bound and appended by ballot.
+                    for (uint32_t i = 0; i < 32u; ++i) {
+                        const uint32_t rr = lane_base + i;
+                        if (m0 + rr >= rows) break;  // padding rows of the last tile
+                        if (sm.rflag[rr]) continue;
+                        uint32_t cnt = sm.rcount[rr];
+                        float rtau = sm.rtau[rr];
+                        const uint32_t col = col0 + lane;
+                        const float x = lane < kChunkCols ? sm.tb[w][lane][i] : kNegInf;
+                        const uint32_t key = total_key(x);
+                        bool take = lane < kChunkCols && col < vocab && x >= rtau;
+                        uint32_t ball = __ballot_sync(0xffffffffu, take);
+                        uint32_t *lkey = sm.ckey[rr];
+                        uint32_t *lidx = sm.cidx[rr];
+                        if (cnt + __popc(ball) > kRowCap) {
+                            // Full: tau rises to the k-th largest of the list and
+                            // the new values together, and both are cut to it.
+                            const uint32_t kth = warp_kth_key(lkey, cnt, key, take, k);
+                            const uint32_t floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
+                            rtau = key_to_float(floor_key);
+                            cnt = warp_compact(lkey, lidx, cnt, floor_key);
+                            take = take && key >= floor_key;
+                            ball = __ballot_sync(0xffffffffu, take);
+                            if (cnt + __popc(ball) > kRowCap) {
+                                // More than kRowCap - k ties at the k-th value:
+                                // the row is left to the unfused path.
+                                if (lane == 0) sm.rflag[rr] = 1u;
+                                __syncwarp();
+                                continue;
+                            }
+                        }
+                        if (take) {
+                            const uint32_t pos = cnt + __popc(ball & ((1u << lane) - 1u));
+                            lkey[pos] = key;
+                            lidx[pos] = col;
+                        }
+                        __syncwarp();
+                        if (lane == 0) {
+                            sm.rcount[rr] = cnt + __popc(ball);
+                            sm.rtau[rr] = rtau;
+                        }
+                        __syncwarp();
                     }
                 }
             }
@@ -307,35 +410,49 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
         }
-        if (kFused && grow < rows) {
-            // The record of (part, row): the part's entries at or above its own
-            // k-th largest value (ties included, at most k + RSC_SHARD_TIE_CAP),
-            // so that the merge's union over many parts stays small.
+        if (kFused) {
+            // The record of each (part, row) of the warp: the part's entries at
+            // or above its own k-th largest value (ties included, at most
+            // k + RSC_SHARD_TIE_CAP), so that merges over many parts stay small.
             const uint32_t cap = k + RSC_SHARD_TIE_CAP;
-            if (!overflow && count >= k) {
-                const uint32_t kth = row_kth_key(sm, r, count, k);
-                const uint32_t floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
-                tau = key_to_float(floor_key);
-                count = row_compact(sm, r, count, floor_key);
-                if (count > cap) overflow = true;
+            for (uint32_t i = 0; i < 32u; ++i) {
+                const uint32_t rr = lane_base + i;
+                const uint32_t gr = m0 + rr;
+                if (gr >= rows) break;
+                uint32_t cnt = sm.rcount[rr];
+                float rtau = sm.rtau[rr];
+                bool ovf = sm.rflag[rr] != 0u;
+                uint32_t *lkey = sm.ckey[rr];
+                uint32_t *lidx = sm.cidx[rr];
+                if (!ovf && cnt >= k) {
+                    const uint32_t kth = warp_kth_key(lkey, cnt, 0u, false, k);
+                    const uint32_t floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
+                    rtau = key_to_float(floor_key);
+                    cnt = warp_compact(lkey, lidx, cnt, floor_key);
+                    if (cnt > cap) ovf = true;
+                }
+                unsigned char *rec = records + (static_cast<size_t>(part) * rows + gr) * rec_bytes;
+                ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
+                uint32_t *ridx = rkey + cap;
+                const uint32_t n = ovf ? 0u : cnt;
+                for (uint32_t e = lane; e < n; e += 32u) {
+                    rkey[e] = lkey[e];
+                    ridx[e] = lidx[e];
+                }
+                const float rmax = __shfl_sync(0xffffffffu, vmax, static_cast<int>(i));
+                if (lane == 0) {
+                    h->max_scaled = rmax;
+                    h->sum_exp = 0.0f;
+                    h->n_finite = 0;
+                    h->n_cand = n;
+                    h->n_dropped = 0;
+                    h->last_key = 0;
+                    h->flags = (ovf || *err) ? 1u : 0u;
+                    h->tau = rtau;
+                }
+                __syncwarp();
             }
-            unsigned char *rec = records + (static_cast<size_t>(part) * rows + grow) * rec_bytes;
-            ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
-            uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
-            uint32_t *ridx = rkey + cap;
-            const uint32_t n = overflow ? 0u : count;
-            for (uint32_t i = 0; i < n; ++i) {
-                rkey[i] = sm.ckey[i][r];
-                ridx[i] = sm.cidx[i][r];
-            }
-            h->max_scaled = vmax;
-            h->sum_exp = 0.0f;
-            h->n_finite = 0;
-            h->n_cand = n;
-            h->n_dropped = 0;
-            h->last_key = 0;
-            h->flags = (overflow || *err) ? 1u : 0u;
-            h->tau = tau;
         }
     }
 

@@ -72,9 +72,11 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
 
 // LM-head GEMM with the sampler fused into its epilogue (lmhead.cu). A row
 // keeps at most kLmheadRowCap candidates per part, so top_k <= kLmheadRowCap -
-// RSC_SHARD_TIE_CAP; a row is spread over at most kLmheadMaxParts parts.
+// RSC_SHARD_TIE_CAP; a row is spread over at most kLmheadMaxParts parts, whose
+// records are reduced in groups until one merge list holds them.
 constexpr uint32_t kLmheadRowCap = 64;
-constexpr uint32_t kLmheadMaxParts = 32;
+constexpr uint32_t kLmheadMaxParts = 256;
+constexpr uint32_t kLmheadRecordSlots = kLmheadMaxParts + 48;  // parts + reduction levels
 uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms);
 // logits != nullptr: writes rows x vocab f32 logits; otherwise writes one
 // shard record per (part, row) into records ([parts][rows], rec_bytes each).
