@@ -280,10 +280,12 @@ RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t rows, size_t
  * each row's top-k candidates in its epilogue and a merge finishes every row;
  * the result equals rsc_sample on the logits rsc_lmhead_logits returns, bit
  * for bit. It requires top-k on with top_k <= 40 and a finite T > 0 (else
- * RSC_ERR_INVALID_ARGUMENT). A row where more than 48 - top_k logits of one
- * vocabulary part tie at that part's k-th value reports RSC_ROW_INTERNAL and
- * is sampled with rsc_lmhead_logits + rsc_sample instead. The first call
- * allocates the handle's LM-head records.
+ * RSC_ERR_INVALID_ARGUMENT), and vocab <= 16777216 (else
+ * RSC_ERR_VOCAB_TOO_LARGE). The vocabulary is split into parts of at most
+ * 65536 columns; a row where, in one part, more than top_k + 24 logits lie at
+ * or above the part's k-th value (heavy ties, e.g. a zero hidden state)
+ * reports RSC_ROW_INTERNAL and is sampled with rsc_lmhead_logits + rsc_sample
+ * instead. The first call allocates the handle's LM-head records.
  */
 RSC_API rsc_status rsc_lmhead_logits(rsc_sampler *sampler, const void *d_hidden,
                                      const void *d_weight, size_t rows, size_t dim, size_t vocab,

@@ -439,7 +439,7 @@ namespace {
 rsc_status check_lmhead(const rsc_sampler *s, const void *d_hidden, const void *d_weight,
                         size_t rows, size_t dim, size_t vocab) {
     if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
-    if (vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (vocab > kMaxVocab || vocab > rsc::kLmheadMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
     if (rows > s->max_rows) return RSC_ERR_CAPACITY;
     if (rows > 0 && (vocab == 0 || dim == 0 || dim % 8 != 0)) return RSC_ERR_INVALID_SHAPE;
     if (dim > (size_t{1} << 30)) return RSC_ERR_INVALID_SHAPE;

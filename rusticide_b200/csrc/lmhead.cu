@@ -32,25 +32,28 @@ namespace rsc {
 namespace {
 
 constexpr int kBM = 128;        // rows of a tile (tensor-memory lanes)
-constexpr int kBN = 256;        // vocab columns of a tile
+constexpr int kBN = 256;        // vocab columns of a full tile
 constexpr int kBK = 64;         // k per stage: 128 bytes of bf16, one swizzle span
 constexpr int kUK = 16;         // k per tcgen05.mma (kind::f16)
+constexpr int kUnit = 16;       // column granularity of parts and tiles (smallest MMA N at M 128)
 constexpr int kGStages = 3;
 constexpr int kGThreads = 192;
-constexpr int kEpiWarp0 = 2;
-constexpr uint32_t kRowCap = kLmheadRowCap;  // candidates a row keeps in shared memory
-constexpr uint32_t kChunkCols = 16;          // accumulator columns per epilogue step
+constexpr uint32_t kListCap = 96;        // candidates a row holds in shared memory per part
+constexpr uint32_t kChunkCols = 16;      // accumulator columns per epilogue step
+constexpr uint32_t kKeyStride = kBM + 1; // list slot stride of the keys (words)
+constexpr uint32_t kIdxStride = kBM + 2; // list slot stride of the indices (halfwords)
 constexpr uint32_t kTmemCols = 2 * kBN;
+constexpr uint32_t kFloorSlack = 8;      // a list cut may keep up to k + 8 entries
+static_assert(kLmheadRowCap <= kListCap - kChunkCols, "a record's candidates fit a list");
 
 struct LmSmem {
     __nv_bfloat16 a[kGStages][kBM * kBK];  // 16 KiB per stage
     __nv_bfloat16 b[kGStages][kBN * kBK];  // 32 KiB per stage
-    uint32_t ckey[kBM][kRowCap];           // per-row candidate lists
-    uint32_t cidx[kBM][kRowCap];
-    float tb[kBM / 32][kChunkCols][33];    // per-warp transpose of a 32-row chunk
-    float rtau[kBM];                       // per-row bound, candidate count, overflow
-    uint32_t rcount[kBM];
-    uint32_t rflag[kBM];
+    // Per-row candidate lists, slot-major (slot s of row r at s * stride + r):
+    // the owning thread appends to its own row, a warp reads one row's slots
+    // without bank conflicts. Indices are relative to the part's first column.
+    uint32_t lkey[kListCap * kKeyStride];
+    uint16_t lidx[kListCap * kIdxStride];
     uint64_t full[kGStages];
     uint64_t empty[kGStages];
     uint64_t acc_full[2];
@@ -60,12 +63,14 @@ struct LmSmem {
 };
 static_assert(sizeof(__nv_bfloat16) * kBM * kBK % 1024 == 0, "stages stay 1024-byte aligned");
 constexpr size_t kLmSmemBytes = sizeof(LmSmem) + 1024;  // + alignment slack
+static_assert(kLmSmemBytes <= 232448, "fits the 227 KiB of shared memory a CTA may use");
 
 // Instruction descriptor of tcgen05.mma kind::f16: f32 accumulator, bf16 A
-// and B, both K-major, N = 256, M = 128 (field layout of the PTX ISA).
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
-                            (static_cast<uint32_t>(kBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kBM >> 4) << 24);
+// and B, both K-major, M = 128, N = n (field layout of the PTX ISA).
+__host__ __device__ constexpr uint32_t idesc_for(uint32_t n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) |
+           (static_cast<uint32_t>(kBM >> 4) << 24);
+}
 
 // Shared-memory matrix descriptor of a K-major tile written by a 128-byte
 // swizzled TMA load: rows of 128 bytes, 8-row groups 1024 bytes apart.
@@ -83,12 +88,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(kIdesc), "r"(acc)
+        "l"(da), "l"(db), "r"(idesc), "r"(acc)
         : "memory");
 }
 
@@ -132,54 +138,78 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// One warp: the k-th largest key over a row's n list entries (n <= 64) and
-// one extra key per lane (where has_extra), by a bitwise search.
-__device__ __forceinline__ uint32_t warp_kth_key(const uint32_t *lkey, uint32_t n, uint32_t extra,
-                                                 bool has_extra, uint32_t k) {
-    const uint32_t lane = threadIdx.x & 31u;
-    const bool va = lane < n, vb = lane + 32u < n;
-    const uint32_t a = va ? lkey[lane] : 0u, b = vb ? lkey[lane + 32u] : 0u;
-    uint32_t res = 0;
-    for (int bit = 31; bit >= 0; --bit) {
-        const uint32_t cand = res | (1u << bit);
-        const uint32_t c = (va && a >= cand ? 1u : 0u) + (vb && b >= cand ? 1u : 0u) +
-                           (has_extra && extra >= cand ? 1u : 0u);
-        if (__reduce_add_sync(0xffffffffu, c) >= k) res = cand;
-    }
-    return res;
+// The columns of a vocabulary part: kUnit-column units split evenly over the
+// parts, so that parts differ by at most one unit; tiles of kBN columns from
+// the part's start, the last one narrower.
+struct PartSpan {
+    uint32_t c0, cend, ntiles;
+};
+__host__ __device__ inline PartSpan part_span(uint32_t vocab, uint32_t part, uint32_t parts) {
+    const uint64_t nunits = (vocab + kUnit - 1) / kUnit;
+    const uint32_t u0 = static_cast<uint32_t>(nunits * part / parts);
+    const uint32_t u1 = static_cast<uint32_t>(nunits * (part + 1) / parts);
+    PartSpan s;
+    s.c0 = u0 * kUnit;
+    s.cend = u1 * kUnit;
+    s.ntiles = (s.cend - s.c0 + kBN - 1) / kBN;
+    return s;
 }
 
-// One warp: keeps a row's list entries at or above floor_key, in place;
-// returns their number.
-__device__ __forceinline__ uint32_t warp_compact(uint32_t *lkey, uint32_t *lidx, uint32_t n,
-                                                 uint32_t floor_key) {
+// One warp cuts row rr's list to the entries whose key is at least a floor
+// with at least k entries at or above it (so the floor is at most the list's
+// k-th largest key). The bitwise search over the key stops as soon as the
+// count at the floor is within k + slack. Returns the floor; n becomes the
+// number of entries kept, in place and in list order.
+__device__ __forceinline__ uint32_t warp_cut_row(uint32_t *lkey, uint16_t *lidx, uint32_t rr,
+                                                 uint32_t &n, uint32_t k, uint32_t slack) {
     const uint32_t lane = threadIdx.x & 31u;
-    const bool va = lane < n, vb = lane + 32u < n;
-    const uint32_t ka = va ? lkey[lane] : 0u, kb = vb ? lkey[lane + 32u] : 0u;
-    const uint32_t ia = va ? lidx[lane] : 0u, ib = vb ? lidx[lane + 32u] : 0u;
-    const bool keep_a = va && ka >= floor_key, keep_b = vb && kb >= floor_key;
-    const uint32_t ba = __ballot_sync(0xffffffffu, keep_a), bb = __ballot_sync(0xffffffffu, keep_b);
+    uint32_t key[3];
+    uint16_t idx[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const uint32_t e = lane + 32u * i;
+        // Key 0 is a negative NaN pattern: never a candidate, never counted.
+        key[i] = e < n ? lkey[e * kKeyStride + rr] : 0u;
+        idx[i] = e < n ? lidx[e * kIdxStride + rr] : static_cast<uint16_t>(0);
+    }
+    uint32_t floor_key = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = floor_key | (1u << bit);
+        const uint32_t c = __reduce_add_sync(0xffffffffu, (key[0] >= cand ? 1u : 0u) +
+                                                              (key[1] >= cand ? 1u : 0u) +
+                                                              (key[2] >= cand ? 1u : 0u));
+        if (c >= k) {
+            floor_key = cand;
+            if (c <= k + slack) break;
+        }
+    }
+    // +0 as the floor would cut -0, which IEEE >= keeps beside +0.
+    if (floor_key == kKeyPosZero) floor_key = kKeyNegZero;
     const uint32_t lt = (1u << lane) - 1u;
+    uint32_t base = 0;
     __syncwarp();
-    if (keep_a) {
-        const uint32_t pos = __popc(ba & lt);
-        lkey[pos] = ka;
-        lidx[pos] = ia;
-    }
-    if (keep_b) {
-        const uint32_t pos = __popc(ba) + __popc(bb & lt);
-        lkey[pos] = kb;
-        lidx[pos] = ib;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const bool keep = key[i] >= floor_key && key[i] != 0u;
+        const uint32_t ball = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            const uint32_t pos = base + __popc(ball & lt);
+            lkey[pos * kKeyStride + rr] = key[i];
+            lidx[pos * kIdxStride + rr] = idx[i];
+        }
+        base += __popc(ball);
     }
     __syncwarp();
-    return __popc(ba) + __popc(bb);
+    n = base;
+    return floor_key;
 }
 
 template <bool kFused>
 __global__ void __launch_bounds__(kGThreads, 1)
 lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
-              uint32_t rows, uint32_t dim, uint32_t vocab, uint32_t n_tiles, CallParams cp,
-              float *__restrict__ logits, unsigned char *__restrict__ records, size_t rec_bytes,
+              const __grid_constant__ CUtensorMap map_w16, uint32_t rows, uint32_t dim,
+              uint32_t vocab, CallParams cp, float *__restrict__ logits, bool vec_out,
+              unsigned char *__restrict__ records, size_t rec_bytes,
               uint32_t *__restrict__ error_out) {
     extern __shared__ unsigned char smem_raw[];
     LmSmem &sm = *reinterpret_cast<LmSmem *>(
@@ -187,8 +217,7 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t part = blockIdx.x, parts = gridDim.x;
     const uint32_t m0 = blockIdx.y * kBM;
-    const uint32_t t0 = static_cast<uint32_t>((static_cast<unsigned long long>(n_tiles) * part) / parts);
-    const uint32_t t1 = static_cast<uint32_t>((static_cast<unsigned long long>(n_tiles) * (part + 1)) / parts);
+    const PartSpan span = part_span(vocab, part, parts);
     const uint32_t kblocks = (dim + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
@@ -220,7 +249,9 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (uint32_t t = t0; t < t1 && ok; ++t) {
+            for (uint32_t t = 0; t < span.ntiles && ok; ++t) {
+                const uint32_t c = span.c0 + t * kBN;
+                const uint32_t w = min(static_cast<uint32_t>(kBN), span.cend - c);
                 for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
                     const uint32_t s = it % kGStages;
                     if (it >= kGStages && !mbar_wait(&sm.empty[s], ((it / kGStages) - 1u) & 1u)) {
@@ -232,12 +263,20 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&sm.full[s],
-                                          static_cast<uint32_t>(sizeof(sm.a[0]) + sizeof(sm.b[0])));
-                    tma_load_2d(sm.a[s], &map_h, &sm.full[s], static_cast<int32_t>(kb * kBK),
-                                static_cast<int32_t>(m0));
-                    tma_load_2d(sm.b[s], &map_w, &sm.full[s], static_cast<int32_t>(kb * kBK),
-                                static_cast<int32_t>(t * kBN));
+                    // Full boxes count their out-of-range (zero-filled) elements.
+                    mbar_arrive_expect_tx(&sm.full[s], static_cast<uint32_t>(sizeof(sm.a[0])) +
+                                                           w * kBK * static_cast<uint32_t>(sizeof(__nv_bfloat16)));
+                    const int32_t x = static_cast<int32_t>(kb * kBK);
+                    tma_load_2d(sm.a[s], &map_h, &sm.full[s], x, static_cast<int32_t>(m0));
+                    if (w == static_cast<uint32_t>(kBN)) {
+                        tma_load_2d(sm.b[s], &map_w, &sm.full[s], x, static_cast<int32_t>(c));
+                    } else {
+                        // A narrow tile: 16-row boxes stacked at 2 KiB steps keep
+                        // the 128-byte swizzle phase of a full box.
+                        for (uint32_t i = 0; i < w / kUnit; ++i)
+                            tma_load_2d(sm.b[s] + i * kUnit * kBK, &map_w16, &sm.full[s], x,
+                                        static_cast<int32_t>(c + i * kUnit));
+                    }
                 }
             }
             // Every copy issued has landed before the CTA moves on (bounded).
@@ -248,9 +287,11 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (uint32_t t = t0, j = 0; t < t1 && ok; ++t, ++j) {
-                const uint32_t buf = j & 1u;
-                if (j >= 2 && !mbar_wait(&sm.acc_empty[buf], ((j >> 1) - 1u) & 1u)) {
+            for (uint32_t t = 0; t < span.ntiles && ok; ++t) {
+                const uint32_t buf = t & 1u;
+                const uint32_t w = min(static_cast<uint32_t>(kBN), span.cend - (span.c0 + t * kBN));
+                const uint32_t idesc = idesc_for(w);
+                if (t >= 2 && !mbar_wait(&sm.acc_empty[buf], ((t >> 1) - 1u) & 1u)) {
                     *err = 1u;
                     break;
                 }
@@ -268,7 +309,7 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
 #pragma unroll
                     for (int kk = 0; kk < kBK / kUK; ++kk) {
                         const uint32_t off = static_cast<uint32_t>(kk * kUK * sizeof(__nv_bfloat16));
-                        mma_bf16(d, smem_desc(sa + off), smem_desc(sb + off), (kb | kk) ? 1u : 0u);
+                        mma_bf16(d, smem_desc(sa + off), smem_desc(sb + off), idesc, (kb | kk) ? 1u : 0u);
                     }
                     mma_commit(&sm.empty[s]);  // the stage is free once these MMAs have read it
                 }
@@ -284,56 +325,68 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
         const uint32_t lane_base = 32u * (static_cast<uint32_t>(warp) & 3u);
         const uint32_t r = lane_base + lane;
         const uint32_t grow = m0 + r;
+        const bool row_ok = grow < rows;
         const float scale = cp.scale;
-        float vmax = kNegInf;  // this thread's row maximum
         const uint32_t k = cp.top_k;
-        // Row state: no candidates, the bound that admits everything but -inf.
-        sm.rcount[r] = 0;
-        sm.rtau[r] = -3.402823466e38f;
-        sm.rflag[r] = 0;
-        __syncwarp();
-        for (uint32_t t = t0, j = 0; t < t1; ++t, ++j) {
-            const uint32_t buf = j & 1u;
-            bool got = mbar_wait(&sm.acc_full[buf], (j >> 1) & 1u);
+        // Row state, in the owning thread's registers: the part's maximum, the
+        // number of listed candidates, and the admission bound (NaN admits
+        // nothing: padding rows and rows whose ties overflowed the list).
+        float vmax = kNegInf;
+        uint32_t cnt = 0;
+        bool ovf = false;
+        float tau = row_ok ? -3.402823466e38f : __int_as_float(0x7fffffff);
+        for (uint32_t t = 0; t < span.ntiles; ++t) {
+            const uint32_t buf = t & 1u;
+            const uint32_t c = span.c0 + t * kBN;
+            const uint32_t w = min(static_cast<uint32_t>(kBN), span.cend - c);
+            bool got = mbar_wait(&sm.acc_full[buf], (t >> 1) & 1u);
             if (__any_sync(0xffffffffu, !got) || *err) {
                 if (lane == 0) *err = 1u;
                 break;
             }
             tc_fence_after();
             if (!kFused) {
-                for (uint32_t c = 0; c < kBN; c += 32) {
+                for (uint32_t cc = 0; cc < w; cc += 32) {
                     uint32_t v[32];
-                    tmem_ld32(tmem + buf * kBN + c + (lane_base << 16), v);
-                    const uint32_t col0 = t * kBN + c;
-                    if (grow < rows) {
+                    tmem_ld32(tmem + buf * kBN + cc + (lane_base << 16), v);
+                    if (row_ok) {
+                        const uint32_t col0 = c + cc;
+                        const uint32_t lim = min(min(32u, w - cc), vocab - min(vocab, col0));
+                        float *dst = logits + static_cast<size_t>(grow) * vocab + col0;
+                        if (vec_out && lim == 32u) {
 #pragma unroll
-                        for (int q = 0; q < 32; ++q)
-                            if (col0 + q < vocab)
-                                logits[static_cast<size_t>(grow) * vocab + col0 + q] = __uint_as_float(v[q]);
+                            for (int q = 0; q < 32; q += 4)
+                                *reinterpret_cast<float4 *>(dst + q) =
+                                    make_float4(__uint_as_float(v[q]), __uint_as_float(v[q + 1]),
+                                                __uint_as_float(v[q + 2]), __uint_as_float(v[q + 3]));
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 32; ++q)
+                                if (static_cast<uint32_t>(q) < lim) dst[q] = __uint_as_float(v[q]);
+                        }
                     }
                 }
             } else {
-                const uint32_t w = static_cast<uint32_t>(warp) & 3u;
-                if (j == 0) {
+                if (t == 0) {
                     // First tile of the part: a starting bound for each row.
-                    // Its 256 columns fall into 48 disjoint groups (column
-                    // within a 16-column step, step mod 3); the smallest of the
-                    // 48 group maxima has 48 distinct values at or above it, so
-                    // it is at most the part's k-th largest value (k <= 48).
+                    // Its columns fall into 48 disjoint groups (column within a
+                    // 16-column step, step mod 3); the smallest of the 48 group
+                    // maxima has 48 distinct values at or above it, so it is at
+                    // most the part's k-th largest value (k <= 48). An empty
+                    // group leaves the bound at -inf.
                     float gm[3][kChunkCols];
 #pragma unroll
                     for (int g = 0; g < 3; ++g)
 #pragma unroll
                         for (int q = 0; q < static_cast<int>(kChunkCols); ++q) gm[g][q] = kNegInf;
-                    for (uint32_t c = 0, step = 0; c < kBN; c += kChunkCols, ++step) {
+                    for (uint32_t cc = 0, step = 0; cc < w; cc += kChunkCols, ++step) {
                         uint32_t v[kChunkCols];
-                        tmem_ld16(tmem + buf * kBN + c + (lane_base << 16), v);
-                        const uint32_t col0 = t * kBN + c;
+                        tmem_ld16(tmem + buf * kBN + cc + (lane_base << 16), v);
                         const uint32_t g = step % 3u;
 #pragma unroll
                         for (int q = 0; q < static_cast<int>(kChunkCols); ++q) {
-                            const float x = col0 + q < vocab ? scale_logit(__uint_as_float(v[q]), scale)
-                                                             : kNegInf;
+                            const float x = c + cc + q < vocab ? scale_logit(__uint_as_float(v[q]), scale)
+                                                               : kNegInf;
                             if (g == 0) gm[0][q] = fmaxf(gm[0][q], x);
                             else if (g == 1) gm[1][q] = fmaxf(gm[1][q], x);
                             else gm[2][q] = fmaxf(gm[2][q], x);
@@ -344,65 +397,51 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
                     for (int g = 0; g < 3; ++g)
 #pragma unroll
                         for (int q = 0; q < static_cast<int>(kChunkCols); ++q) b = fminf(b, gm[g][q]);
-                    if (grow < rows && k <= 3u * kChunkCols && b > sm.rtau[r]) sm.rtau[r] = b;
-                    __syncwarp();
+                    if (k <= 3u * kChunkCols && b > tau) tau = b;
                 }
-                for (uint32_t c = 0; c < kBN; c += kChunkCols) {
-                    uint32_t v[kChunkCols];
-                    tmem_ld16(tmem + buf * kBN + c + (lane_base << 16), v);
-                    const uint32_t col0 = t * kBN + c;
-                    // Thread = row: scale, track the row maximum, and transpose
-                    // the 32 x 16 block through shared memory.
-#pragma unroll
-                    for (int q = 0; q < static_cast<int>(kChunkCols); ++q) {
-                        const float x = scale_logit(__uint_as_float(v[q]), scale);
-                        if (col0 + q < vocab) vmax = fmaxf(vmax, x);
-                        sm.tb[w][q][lane] = x;
-                    }
-                    __syncwarp();
-                    // Warp = row: the 16 values of each of the warp's rows in
-                    // turn, filtered by the row's bound and appended by ballot.
-                    for (uint32_t i = 0; i < 32u; ++i) {
-                        const uint32_t rr = lane_base + i;
-                        if (m0 + rr >= rows) break;  // padding rows of the last tile
-                        if (sm.rflag[rr]) continue;
-                        uint32_t cnt = sm.rcount[rr];
-                        float rtau = sm.rtau[rr];
-                        const uint32_t col = col0 + lane;
-                        const float x = lane < kChunkCols ? sm.tb[w][lane][i] : kNegInf;
-                        const uint32_t key = total_key(x);
-                        bool take = lane < kChunkCols && col < vocab && x >= rtau;
-                        uint32_t ball = __ballot_sync(0xffffffffu, take);
-                        uint32_t *lkey = sm.ckey[rr];
-                        uint32_t *lidx = sm.cidx[rr];
-                        if (cnt + __popc(ball) > kRowCap) {
-                            // Full: tau rises to the k-th largest of the list and
-                            // the new values together, and both are cut to it.
-                            const uint32_t kth = warp_kth_key(lkey, cnt, key, take, k);
-                            const uint32_t floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
-                            rtau = key_to_float(floor_key);
-                            cnt = warp_compact(lkey, lidx, cnt, floor_key);
-                            take = take && key >= floor_key;
-                            ball = __ballot_sync(0xffffffffu, take);
-                            if (cnt + __popc(ball) > kRowCap) {
-                                // More than kRowCap - k ties at the k-th value:
-                                // the row is left to the unfused path.
-                                if (lane == 0) sm.rflag[rr] = 1u;
-                                __syncwarp();
-                                continue;
+                for (uint32_t cc = 0; cc < w; cc += kChunkCols) {
+                    // Room for a whole chunk: rows near the cap are cut first,
+                    // one at a time by the whole warp.
+                    uint32_t need = __ballot_sync(0xffffffffu, !ovf && cnt > kListCap - kChunkCols);
+                    while (need) {
+                        const int i = __ffs(need) - 1;
+                        need &= need - 1u;
+                        uint32_t n = __shfl_sync(0xffffffffu, cnt, i);
+                        const uint32_t fk = warp_cut_row(sm.lkey, sm.lidx, lane_base + i, n, k, kFloorSlack);
+                        if (lane == i) {
+                            cnt = n;
+                            const float f = key_to_float(fk);
+                            if (f > tau) tau = f;
+                            if (cnt > kListCap - kChunkCols) {
+                                // More ties at the k-th value than the list
+                                // holds: the row is reported, not sampled.
+                                ovf = true;
+                                tau = __int_as_float(0x7fffffff);
                             }
                         }
-                        if (take) {
-                            const uint32_t pos = cnt + __popc(ball & ((1u << lane) - 1u));
-                            lkey[pos] = key;
-                            lidx[pos] = col;
+                    }
+                    uint32_t v[kChunkCols];
+                    tmem_ld16(tmem + buf * kBN + cc + (lane_base << 16), v);
+                    const uint32_t col0 = c + cc;
+                    float x[kChunkCols];
+                    bool any = false;
+#pragma unroll
+                    for (int q = 0; q < static_cast<int>(kChunkCols); ++q) {
+                        x[q] = scale_logit(__uint_as_float(v[q]), scale);
+                        if (col0 + q < vocab) {
+                            vmax = fmaxf(vmax, x[q]);
+                            any |= x[q] >= tau;
                         }
-                        __syncwarp();
-                        if (lane == 0) {
-                            sm.rcount[rr] = cnt + __popc(ball);
-                            sm.rtau[rr] = rtau;
+                    }
+                    if (any) {
+#pragma unroll
+                        for (int q = 0; q < static_cast<int>(kChunkCols); ++q) {
+                            if (col0 + q < vocab && x[q] >= tau) {
+                                sm.lkey[cnt * kKeyStride + r] = total_key(x[q]);
+                                sm.lidx[cnt * kIdxStride + r] = static_cast<uint16_t>(col0 + q - span.c0);
+                                ++cnt;
+                            }
                         }
-                        __syncwarp();
                     }
                 }
             }
@@ -412,44 +451,43 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
         }
         if (kFused) {
             // The record of each (part, row) of the warp: the part's entries at
-            // or above its own k-th largest value (ties included, at most
-            // k + RSC_SHARD_TIE_CAP), so that merges over many parts stay small.
+            // or above a floor no higher than its own k-th largest value (ties
+            // included, at most k + RSC_SHARD_TIE_CAP), so that merges over
+            // many parts stay small.
             const uint32_t cap = k + RSC_SHARD_TIE_CAP;
+            __syncwarp();
             for (uint32_t i = 0; i < 32u; ++i) {
                 const uint32_t rr = lane_base + i;
                 const uint32_t gr = m0 + rr;
                 if (gr >= rows) break;
-                uint32_t cnt = sm.rcount[rr];
-                float rtau = sm.rtau[rr];
-                bool ovf = sm.rflag[rr] != 0u;
-                uint32_t *lkey = sm.ckey[rr];
-                uint32_t *lidx = sm.cidx[rr];
-                if (!ovf && cnt >= k) {
-                    const uint32_t kth = warp_kth_key(lkey, cnt, 0u, false, k);
-                    const uint32_t floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
-                    rtau = key_to_float(floor_key);
-                    cnt = warp_compact(lkey, lidx, cnt, floor_key);
-                    if (cnt > cap) ovf = true;
+                uint32_t n = __shfl_sync(0xffffffffu, cnt, static_cast<int>(i));
+                bool o = __shfl_sync(0xffffffffu, ovf ? 1u : 0u, static_cast<int>(i)) != 0u;
+                float rt = __shfl_sync(0xffffffffu, tau, static_cast<int>(i));
+                const float rmax = __shfl_sync(0xffffffffu, vmax, static_cast<int>(i));
+                if (!o && n > cap) {
+                    const uint32_t fk = warp_cut_row(sm.lkey, sm.lidx, rr, n, k, kFloorSlack);
+                    const float f = key_to_float(fk);
+                    if (f > rt) rt = f;
+                    if (n > cap) o = true;
                 }
                 unsigned char *rec = records + (static_cast<size_t>(part) * rows + gr) * rec_bytes;
                 ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
                 uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
                 uint32_t *ridx = rkey + cap;
-                const uint32_t n = ovf ? 0u : cnt;
-                for (uint32_t e = lane; e < n; e += 32u) {
-                    rkey[e] = lkey[e];
-                    ridx[e] = lidx[e];
+                const uint32_t nw = o ? 0u : n;
+                for (uint32_t e = lane; e < nw; e += 32u) {
+                    rkey[e] = sm.lkey[e * kKeyStride + rr];
+                    ridx[e] = span.c0 + sm.lidx[e * kIdxStride + rr];
                 }
-                const float rmax = __shfl_sync(0xffffffffu, vmax, static_cast<int>(i));
                 if (lane == 0) {
                     h->max_scaled = rmax;
                     h->sum_exp = 0.0f;
                     h->n_finite = 0;
-                    h->n_cand = n;
+                    h->n_cand = nw;
                     h->n_dropped = 0;
                     h->last_key = 0;
-                    h->flags = (ovf || *err) ? 1u : 0u;
-                    h->tau = rtau;
+                    h->flags = (o || *err) ? 1u : 0u;
+                    h->tau = o ? -3.402823466e38f : rt;
                 }
                 __syncwarp();
             }
@@ -506,8 +544,13 @@ uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms) {
     const uint32_t ntiles = (vocab + kBN - 1) / kBN;
     size_t p = mtiles ? static_cast<size_t>(num_sms) / mtiles : 1;
     if (p < 1) p = 1;
-    if (p > kLmheadMaxParts) p = kLmheadMaxParts;
     if (p > ntiles) p = ntiles;
+    // Candidate indices are kept relative to the part's first column in 16
+    // bits: no part spans more than 65536 columns.
+    const size_t nunits = (vocab + kUnit - 1) / kUnit;
+    const size_t min_parts = (nunits + 4095) / 4096;
+    if (p < min_parts) p = min_parts;
+    if (p > kLmheadMaxParts) p = kLmheadMaxParts;
     return static_cast<uint32_t>(p);
 }
 
@@ -516,18 +559,21 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
                           size_t rec_bytes, uint32_t parts, uint32_t *error_flag,
                           cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
-    CUtensorMap mh, mw;
-    if (!make_map(&mh, hidden, rows, dim, kBM) || !make_map(&mw, weight, vocab, dim, kBN))
+    if ((static_cast<uint64_t>(vocab) + kUnit - 1) / kUnit > static_cast<uint64_t>(parts) * 4096u)
+        return cudaErrorInvalidValue;  // a part would span more than 65536 columns
+    CUtensorMap mh, mw, mw16;
+    if (!make_map(&mh, hidden, rows, dim, kBM) || !make_map(&mw, weight, vocab, dim, kBN) ||
+        !make_map(&mw16, weight, vocab, dim, kUnit))
         return cudaErrorInvalidValue;
-    const uint32_t ntiles = (vocab + kBN - 1) / kBN;
     const dim3 grid(parts, static_cast<unsigned>((rows + kBM - 1) / kBM), 1);
     if (logits) {
         cudaError_t e = cudaFuncSetAttribute(lmhead_kernel<false>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kLmSmemBytes));
         if (e != cudaSuccess) return e;
+        const bool vec = vocab % 4 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
         lmhead_kernel<false><<<grid, kGThreads, kLmSmemBytes, stream>>>(
-            mh, mw, static_cast<uint32_t>(rows), dim, vocab, ntiles, p, logits, nullptr, 0,
+            mh, mw, mw16, static_cast<uint32_t>(rows), dim, vocab, p, logits, vec, nullptr, 0,
             error_flag);
     } else {
         cudaError_t e = cudaFuncSetAttribute(lmhead_kernel<true>,
@@ -535,7 +581,7 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
                                              static_cast<int>(kLmSmemBytes));
         if (e != cudaSuccess) return e;
         lmhead_kernel<true><<<grid, kGThreads, kLmSmemBytes, stream>>>(
-            mh, mw, static_cast<uint32_t>(rows), dim, vocab, ntiles, p, nullptr,
+            mh, mw, mw16, static_cast<uint32_t>(rows), dim, vocab, p, nullptr, false,
             static_cast<unsigned char *>(records), rec_bytes, error_flag);
     }
     return cudaGetLastError();

@@ -70,12 +70,15 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, uint32_t *scratch, uint32_t slots, cudaStream_t stream);
 
-// LM-head GEMM with the sampler fused into its epilogue (lmhead.cu). A row
-// keeps at most kLmheadRowCap candidates per part, so top_k <= kLmheadRowCap -
-// RSC_SHARD_TIE_CAP; a row is spread over at most kLmheadMaxParts parts, whose
-// records are reduced in groups until one merge list holds them.
+// LM-head GEMM with the sampler fused into its epilogue (lmhead.cu). A part's
+// record of a row holds at most kLmheadRowCap candidates, so top_k <=
+// kLmheadRowCap - RSC_SHARD_TIE_CAP; a row is spread over at most
+// kLmheadMaxParts parts of at most 65536 columns each (vocab <=
+// kLmheadMaxVocab), whose records are reduced in groups until one merge list
+// holds them.
 constexpr uint32_t kLmheadRowCap = 64;
 constexpr uint32_t kLmheadMaxParts = 256;
+constexpr uint64_t kLmheadMaxVocab = uint64_t{kLmheadMaxParts} * 65536u;
 constexpr uint32_t kLmheadRecordSlots = kLmheadMaxParts + 48;  // parts + reduction levels
 uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms);
 // logits != nullptr: writes rows x vocab f32 logits; otherwise writes one

@@ -84,3 +84,23 @@ def test_lmhead_rejects_unsupported_params(eng):
             eng.lmhead_sample(h, w, params, uniforms=u)
     with pytest.raises(SamplingError):
         eng.lmhead_logits(h.float(), w)
+
+
+def test_lmhead_tied_row_reports_internal(eng):
+    """A zero hidden state makes every logit of its row +0: each vocabulary
+    part ties far beyond its record's capacity, so the row reports
+    RSC_ROW_INTERNAL (to be resampled from rsc_lmhead_logits + rsc_sample),
+    and the other rows of the batch are unaffected."""
+    from rusticide_b200 import _lib
+    h, w = _inputs(4, 256, 4096, seed=3)
+    h[2] = 0
+    params = SamplingParams(0.8, 40, 0.95)
+    u = torch.rand(4, device="cuda")
+    ids_f, st_f, pr_f = eng.lmhead_sample(h, w, params, uniforms=u)
+    ids_s, st_s, pr_s = eng.sample(eng.lmhead_logits(h, w), params, uniforms=u)
+    torch.cuda.synchronize()
+    assert int(st_f[2]) & 0xFF == _lib.RSC_ROW_INTERNAL
+    keep = torch.tensor([0, 1, 3], device="cuda")
+    assert torch.equal(st_f[keep], st_s[keep])
+    assert torch.equal(ids_f[keep], ids_s[keep])
+    assert torch.equal(pr_f[keep].view(torch.int32), pr_s[keep].view(torch.int32))
