@@ -115,6 +115,24 @@ RSC_API rsc_status rsc_sample(rsc_sampler *sampler, const float *d_logits, size_
                       float *d_out_probs, void *stream);
 
 /*
+ * rsc_sample with one parameter set per row, as a batch of sequences with
+ * their own SamplingParams has it: row r is Sampler::sample_logits(row r,
+ * h_params[r]) (src/sampler.rs:44-54), with the same outputs and uniforms as
+ * rsc_sample. h_params is a HOST array of rows sets, copied to the device
+ * before the call returns (the caller may reuse it at once). One launch: a
+ * row whose set the streaming top-k filter cannot serve (top-k off over more
+ * than 512 logits, top_k > 128, or T = inf) is sampled whole in the same
+ * launch, at the large-survivor path's speed. The first call allocates the
+ * handle's parameter buffers; a call waits for the previous call's parameter
+ * copy to have left the host.
+ */
+RSC_API rsc_status rsc_sample_rows(rsc_sampler *sampler, const float *d_logits, size_t rows,
+                                   size_t vocab, size_t row_stride, const rsc_params *h_params,
+                                   const float *d_uniforms, uint64_t *d_rng_states,
+                                   uint32_t *d_out_ids, int32_t *d_out_status,
+                                   float *d_out_probs, void *stream);
+
+/*
  * Optional outputs of rsc_sample_ex: the candidate set that survived top-k and
  * top-p (the reference's Candidates after Candidates::filter,
  * src/candidates.rs:16-22), per row, in index order.

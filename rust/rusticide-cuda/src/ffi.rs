@@ -69,6 +69,20 @@ unsafe extern "C" {
         d_out_probs: *mut f32,
         stream: *mut c_void,
     ) -> c_int;
+    pub(crate) fn rsc_sample_rows(
+        sampler: *mut RscSampler,
+        d_logits: *const f32,
+        rows: usize,
+        vocab: usize,
+        row_stride: usize,
+        h_params: *const RscParams,
+        d_uniforms: *const f32,
+        d_rng_states: *mut u64,
+        d_out_ids: *mut u32,
+        d_out_status: *mut i32,
+        d_out_probs: *mut f32,
+        stream: *mut c_void,
+    ) -> c_int;
     pub(crate) fn rsc_sample_ex(
         sampler: *mut RscSampler,
         d_logits: *const f32,

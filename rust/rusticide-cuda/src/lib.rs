@@ -263,6 +263,52 @@ impl CudaSampler {
         check(if pick { "rsc_pick" } else { "rsc_sample" }, code)
     }
 
+    /// Batched `sample_logits` on device rows with one `SamplingParams` per
+    /// row (`params[r]` for row `r`), asynchronous on `stream`; the sets are
+    /// copied before the call returns.
+    ///
+    /// # Safety
+    ///
+    /// As [`CudaSampler::sample_device`], with `params.len() == rows`.
+    ///
+    /// # Errors
+    ///
+    /// `CudaError` for a rejected argument or a launch failure.
+    #[allow(clippy::too_many_arguments)]
+    pub unsafe fn sample_rows_device(
+        &mut self,
+        d_logits: *const f32,
+        rows: usize,
+        vocab: usize,
+        row_stride: usize,
+        params: &[SamplingParams],
+        d_uniforms: *const f32,
+        d_rng_states: *mut u64,
+        d_ids: *mut u32,
+        d_status: *mut i32,
+        d_probs: *mut f32,
+        stream: *mut c_void,
+    ) -> Result<(), CudaError> {
+        if params.len() != rows {
+            return Err(CudaError::Call {
+                what: "rsc_sample_rows",
+                code: ffi::RSC_ERR_INVALID_SHAPE,
+                name: status_name(ffi::RSC_ERR_INVALID_SHAPE),
+            });
+        }
+        let c: Vec<ffi::RscParams> = params.iter().map(to_c).collect();
+        // SAFETY: `c` holds `rows` sets and outlives the call (the library
+        // copies them before returning); the caller's contract covers the
+        // device pointers; the handle is live and exclusively borrowed.
+        let code = unsafe {
+            ffi::rsc_sample_rows(
+                self.raw.as_ptr(), d_logits, rows, vocab, row_stride, c.as_ptr(), d_uniforms,
+                d_rng_states, d_ids, d_status, d_probs, stream,
+            )
+        };
+        check("rsc_sample_rows", code)
+    }
+
     /// Batched `greedy_logits` on device rows, asynchronous on `stream`.
     ///
     /// # Safety

@@ -67,6 +67,8 @@ SIGNATURES = {
     "rsc_sampler_create": (_ST, [ctypes.c_int, _SZ, _SZ, ctypes.POINTER(_P)]),
     "rsc_sampler_destroy": (_ST, [_P]),
     "rsc_sample": (_ST, [_P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P, _P]),
+    "rsc_sample_rows": (_ST, [_P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P,
+                             _P]),
     "rsc_sample_ex": (_ST, [_P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P,
                             _P, _P]),
     "rsc_greedy": (_ST, [_P, _P, _SZ, _SZ, _SZ, _P, _P, _P]),

@@ -3,10 +3,12 @@
 //
 // Routing of rsc_sample (Sampler::sample_logits):
 //  - scale finite and > 0, and top-k on or vocab <= kSmallCap: the streaming
-//    top-k kernel; rows whose survivors overflow its shared-memory list are
-//    appended to a device list that the large-survivor kernel, launched right
-//    after on the same stream, drains (no host round trip);
+//    top-k kernel; a row whose survivors overflow its shared-memory list is
+//    sampled whole in the epilogue of the CTA that finished it (same launch);
 //  - otherwise every row goes to the large-survivor kernel.
+// rsc_sample_rows (one parameter set per row) always takes the streaming
+// kernel: each row reads its own set, and a row the filter cannot serve is
+// sampled whole in a CTA epilogue.
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -38,6 +40,12 @@ struct rsc_sampler {
     int32_t *stage_status = nullptr;
     float *stage_probs = nullptr;
     cudaStream_t host_stream = nullptr;
+    // Per-row parameter sets of rsc_sample_rows (on first use): pinned host
+    // staging, its device copy, and an event marking the copy's completion.
+    rsc_params *rows_host = nullptr;
+    rsc_params *rows_dev = nullptr;
+    cudaEvent_t rows_copied = nullptr;
+    bool rows_pending = false;
     uint64_t launches = 0;
     bool alive = false;
 };
@@ -94,6 +102,7 @@ rsc::CallParams make_params(const rsc_params &p, size_t vocab, const float *unif
     cp.out_nsurv = nullptr;
     cp.out_surv = nullptr;
     cp.surv_cap = 0;
+    cp.row_params = nullptr;
     return cp;
 }
 
@@ -104,8 +113,13 @@ rsc::CallParams rows_from(const rsc::CallParams &cp, size_t r0) {
     if (b.rng_states) b.rng_states += r0;
     if (b.out_nsurv) b.out_nsurv += r0;
     if (b.out_surv) b.out_surv += r0 * b.surv_cap;
+    if (b.row_params) b.row_params += r0;
     return b;
 }
+
+rsc_status stream_impl(rsc_sampler *s, const float *logits, size_t rows, uint32_t v,
+                       size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
+                       int32_t *status, float *probs, cudaStream_t stream);
 
 rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t vocab,
                        size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
@@ -116,9 +130,21 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
                        ((cp.topk_active && cp.top_k <= rsc::kSmallTopK) ||
                         (!cp.topk_active && vocab <= rsc::kSmallCap));
     cudaError_t e;
-    if (small) {
-        // One launch per batch of at most kStreamRowsPerCta rows per CTA (a
-        // single launch for every batch that fits the GPU this many times).
+    if (small) return stream_impl(s, logits, rows, v, row_stride, cp, ids, status, probs, stream);
+    e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
+                          s->large_slots, stream);
+    ++s->launches;
+    return cuda_status(e);
+}
+
+// The streaming kernel over a call's rows: one launch per batch of at most
+// kStreamRowsPerCta rows per CTA (a single launch for every batch that fits
+// the GPU this many times).
+rsc_status stream_impl(rsc_sampler *s, const float *logits, size_t rows, uint32_t v,
+                       size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
+                       int32_t *status, float *probs, cudaStream_t stream) {
+    cudaError_t e;
+    {
         const size_t batch = static_cast<size_t>(s->num_sms) * 3u * rsc::kStreamRowsPerCta;
         for (size_t r0 = 0; r0 < rows; r0 += batch) {
             const size_t nr = rows - r0 < batch ? rows - r0 : batch;
@@ -141,10 +167,6 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
         }
         return RSC_OK;
     }
-    e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
-                          s->large_slots, stream);
-    ++s->launches;
-    return cuda_status(e);
 }
 
 rsc_status greedy_impl(rsc_sampler *s, const float *logits, size_t rows, size_t vocab,
@@ -242,6 +264,12 @@ rsc_status rsc_sampler_destroy(rsc_sampler *s) {
     cudaFree(s->stage_status);
     cudaFree(s->stage_probs);
     if (s->host_stream) cudaStreamDestroy(s->host_stream);
+    if (s->rows_copied) {
+        cudaEventSynchronize(s->rows_copied);
+        cudaEventDestroy(s->rows_copied);
+    }
+    cudaFreeHost(s->rows_host);
+    cudaFree(s->rows_dev);
     s->alive = false;
     delete s;
     return RSC_OK;
@@ -266,6 +294,53 @@ rsc_status rsc_sample_ex(rsc_sampler *s, const float *d_logits, size_t rows, siz
     DeviceGuard guard(s->device);
     return sample_impl(s, d_logits, rows, vocab, row_stride, cp, d_out_ids, d_out_status,
                        d_out_probs, static_cast<cudaStream_t>(stream));
+}
+
+rsc_status rsc_sample_rows(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,
+                           size_t row_stride, const rsc_params *h_params, const float *d_uniforms,
+                           uint64_t *d_rng_states, uint32_t *d_out_ids, int32_t *d_out_status,
+                           float *d_out_probs, void *stream) {
+    rsc_status st = check_shape(s, d_logits, rows, vocab, row_stride);
+    if (st != RSC_OK) return st;
+    if (rows == 0) return RSC_OK;
+    if (!h_params || !d_out_ids || !d_out_status) return RSC_ERR_INVALID_ARGUMENT;
+    if (vocab == 0) return RSC_ERR_INVALID_SHAPE;
+    // The call-wide schedule is planned for the largest top-k among the rows
+    // the streaming filter serves; every other row is sampled whole.
+    uint32_t max_k = 0;
+    bool draws = false;
+    for (size_t r = 0; r < rows; ++r) {
+        const rsc::CallParams q = make_params(h_params[r], vocab, nullptr, nullptr);
+        if (!q.argmax_branch) draws = true;
+        if (q.normal_scale && q.topk_active && q.top_k <= rsc::kSmallTopK && q.top_k > max_k)
+            max_k = q.top_k;
+    }
+    if (draws && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    if (!s->rows_host) {
+        if (cudaHostAlloc(reinterpret_cast<void **>(&s->rows_host), s->max_rows * sizeof(rsc_params),
+                          cudaHostAllocDefault) != cudaSuccess)
+            return RSC_ERR_CUDA;
+        if (cudaMalloc(&s->rows_dev, s->max_rows * sizeof(rsc_params)) != cudaSuccess)
+            return RSC_ERR_CUDA;
+        if (cudaEventCreateWithFlags(&s->rows_copied, cudaEventDisableTiming) != cudaSuccess)
+            return RSC_ERR_CUDA;
+    }
+    // The staging buffer is rewritten only once the previous call's copy
+    // has read it.
+    if (s->rows_pending && cudaEventSynchronize(s->rows_copied) != cudaSuccess) return RSC_ERR_CUDA;
+    std::memcpy(s->rows_host, h_params, rows * sizeof(rsc_params));
+    if (cudaMemcpyAsync(s->rows_dev, s->rows_host, rows * sizeof(rsc_params),
+                        cudaMemcpyHostToDevice, strm) != cudaSuccess ||
+        cudaEventRecord(s->rows_copied, strm) != cudaSuccess)
+        return RSC_ERR_CUDA;
+    s->rows_pending = true;
+    rsc_params plan_params{1.0f, max_k, 1.0f, 1.0f, 0};
+    rsc::CallParams cp = make_params(plan_params, vocab, d_uniforms, d_rng_states);
+    cp.row_params = s->rows_dev;
+    return stream_impl(s, d_logits, rows, static_cast<uint32_t>(vocab), row_stride, cp, d_out_ids,
+                       d_out_status, d_out_probs, strm);
 }
 
 rsc_status rsc_sample(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,

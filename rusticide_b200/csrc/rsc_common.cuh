@@ -198,7 +198,26 @@ struct CallParams {
     uint32_t *out_nsurv;     // nullable: survivor count per row
     uint32_t *out_surv;      // nullable: rows x surv_cap survivor ids
     uint32_t surv_cap;
+    const rsc_params *row_params = nullptr;  // one parameter set per row (rsc_sample_rows)
 };
+
+// The parameters that apply to one row: the call's, or the row's own set,
+// derived field by field as the host derives the call's.
+__device__ __forceinline__ CallParams for_row(const CallParams &cp, size_t row, size_t vocab) {
+    if (!cp.row_params) return cp;
+    CallParams r = cp;
+    const rsc_params q = cp.row_params[row];
+    r.temperature = q.temperature;
+    // candidates.rs:25-29: 1/T for T > 0, else 1 (IEEE division, as on the host).
+    r.scale = q.temperature > 0.0f ? __fdiv_rn(1.0f, q.temperature) : 1.0f;
+    r.top_k = q.top_k;
+    r.top_p = q.top_p;
+    r.topk_active = q.top_k != 0 && static_cast<size_t>(q.top_k) < vocab;
+    r.topp_active = q.top_p < 1.0f;
+    r.argmax_branch = q.temperature == 0.0f || q.top_k == 1;
+    r.normal_scale = isfinite(r.scale) && r.scale > 0.0f;
+    return r;
+}
 
 // The uniform for a row that takes the draw branch.
 __device__ __forceinline__ float row_uniform(const CallParams &p, size_t row) {

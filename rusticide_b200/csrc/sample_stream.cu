@@ -774,18 +774,28 @@ __device__ __forceinline__ void defer_row(StreamSmem &sm, size_t row, uint32_t *
     }
 }
 
+// Whether the streaming filter serves a row with parameters r (the host's
+// routing rule for a whole call, applied to one row).
+__device__ __forceinline__ bool streams_row(const CallParams &r, uint32_t vocab) {
+    return r.mode == kModeSampleLogits && r.normal_scale &&
+           ((r.topk_active && r.top_k <= kSmallTopK) || (!r.topk_active && vocab <= kSmallCap));
+}
+
 // The epilogue's per-row work, kept out of line so that the large-row code's
 // register pressure stays out of the streaming loops.
 __device__ __noinline__ void epilogue_row(const CallParams &cp, const float *p, uint32_t vocab,
                                           size_t row, uint32_t *scratch, uint32_t *out_ids,
                                           int32_t *out_status, float *out_probs,
                                           large::LargeSmem<kThreads> &ls) {
-    large::sample_row<kThreads>(cp, p, vocab, row, scratch, out_ids, out_status, out_probs, ls);
+    large::sample_row<kThreads>(for_row(cp, row, vocab), p, vocab, row, scratch, out_ids, out_status,
+                                out_probs, ls);
 }
 
 // --- the streaming kernel -------------------------------------------------------
 
-template <bool kRecord>
+// kRows: one parameter set per row (cp.row_params); a separate instance, so
+// that calls with one set for every row pay nothing for the lookups.
+template <bool kRecord, bool kRows = false>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab,
                    size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
@@ -829,18 +839,26 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
     // waits end their roles, and every role meets in the epilogue).
     auto consume = [&]() {
         const int cw = warp;
-        const float scale = cp.scale;
-        const uint32_t t_bound = cp.topk_active ? (cp.top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
         uint32_t consumed = 0, par = 0;
         Piece pc;
         for (uint32_t j = 0; get_piece(rows, nch, streamk, j, pc); ++j) {
             const size_t row = pc.row;
             const uint32_t b = j & 1u;
+            // The row's parameters. A row with its own parameter set that the
+            // streaming filter cannot serve (no top-k over a long row, k above
+            // kSmallTopK, T = inf) is marked overflowing from the start: its
+            // chunks pass through unfiltered and the epilogue samples it.
+            const CallParams rp = kRows ? for_row(cp, row, vocab) : cp;
+            const bool live = !kRows || streams_row(rp, vocab);
+            const float scale = rp.scale;
+            const uint32_t top_k = rp.top_k;
+            const uint32_t t_bound =
+                live && rp.topk_active ? (top_k + kConsumerWarps - 1) / kConsumerWarps : 0u;
             bool bad = false;
             if (threadIdx.x == 0) {
                 if (j >= 2 && !mbar_wait(&sm.list_empty[b], ((j >> 1) - 1u) & 1u)) bad = true;
                 sm.count[b] = 0;
-                sm.overflow[b] = 0;
+                sm.overflow[b] = live ? 0u : 1u;
             }
             if (consumers_any(bad || *static_cast<volatile uint32_t *>(&sm.error) != 0)) break;
             CandList &L = sm.list[b];
@@ -852,7 +870,8 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
             // NaN (NaN reads as -inf in the reference, and -inf never survives);
             // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
-            float tau = -3.402823466e38f;
+            // NaN admits nothing (a row left to the epilogue).
+            float tau = live ? -3.402823466e38f : __int_as_float(0x7fffffff);
             float lmax = kNegInf;  // this lane's largest scaled logit of the piece
             // Scalar head and tail (at most 3 logits each).
             {
@@ -896,14 +915,14 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     }
                     tau = fmaxf(tau, read_bound(sm, par));
                     par ^= 1u;
-                    if (len < kChunk && len >= cp.top_k) {
+                    if (len < kChunk && len >= top_k) {
                         // A partial first chunk (a row's tail part, or a short
                         // row) spreads too thin over the lanes for their maxima
                         // to bound the k-th largest value: take the chunk's own
                         // exact k-th largest instead (the stage is still held).
                         const float *ring = sm.ring[s];
                         const uint32_t kth = group_select_kth_largest<kConsumers, ConsumerSync>(
-                            len, cp.top_k,
+                            len, top_k,
                             [&](uint32_t i) { return total_key(scale_logit(ring[i], scale)); },
                             sm.chist, sm.csel);
                         tau = fmaxf(tau, key_to_float(kth));
@@ -960,7 +979,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 // One barrier per refresh: settles the list, publishes
                 // the bounds, and raises the rare events (a failed wait, a long
                 // list).
-                const bool want_compact = mark && cp.topk_active && !last;
+                const bool want_compact = mark && rp.topk_active && !last;
                 mark = false;
                 if (consumers_any(!got || want_compact)) {
                     if (consumers_any(!got)) {
@@ -969,9 +988,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     }
                     // Compaction: tau rises to the list's own k-th largest value.
                     const uint32_t cnt = min(*count, kCap);
-                    if (cnt >= cp.top_k) {
+                    if (cnt >= top_k) {
                         const uint32_t kth = group_select_kth_largest<kConsumers, ConsumerSync>(
-                            cnt, cp.top_k, [&](uint32_t i) { return L.key[i]; }, sm.chist, sm.csel);
+                            cnt, top_k, [&](uint32_t i) { return L.key[i]; }, sm.chist, sm.csel);
                         tau = fmaxf(tau, key_to_float(kth));
                         constexpr int kPer = kCap / kConsumers;
                         uint32_t kk[kPer], ii[kPer];
@@ -1048,6 +1067,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         Piece pc;
         for (; get_piece(rows, nch, streamk, u, pc); ++u) {
             const size_t row = pc.row;
+            const CallParams rp = kRows ? for_row(cp, row, vocab) : cp;
             const uint32_t j = u;
             const uint32_t b = j & 1u;
             const bool got = mbar_wait(&sm.list_full[b], (j >> 1) & 1u);
@@ -1057,7 +1077,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             }
             uint32_t cnt = sm.count[b];
             const bool ov = sm.overflow[b] != 0 || cnt > kCap;
-            if (!ov && cp.topk_active) cnt = precut_list(sm.list[b], cnt, sm.tau_final[b]);
+            if (!ov && rp.topk_active) cnt = precut_list(sm.list[b], cnt, sm.tau_final[b]);
             if (kRecord) {
                 unsigned char *rec = records + row * rec_bytes;
                 if (ov) {
@@ -1077,7 +1097,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 if (ov) {
                     if (lane == 0) defer_row(sm, row, out_ids, out_status);
                 } else {
-                    finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, cnt, cp, row,
+                    finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, cnt, rp, row,
                                 out_ids, out_status, out_probs);
                 }
             } else {
@@ -1092,7 +1112,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                         h->flags = 1;
                     }
                 } else {
-                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, cp, 0.0f, 0.0f, 0u, rec,
+                    record_list(sm.fw, sm.list[b].key, sm.list[b].idx, cnt, rp, 0.0f, 0.0f, 0u, rec,
                                 seg_cap, sm.tau_final[b]);
                 }
                 __threadfence();
@@ -1106,11 +1126,11 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     const uint32_t n = merge_records(
                         sm.list[b], sm.fw,
                         [&](uint32_t part) { return seg_records + (row * max_parts + part) * rec_bytes; },
-                        pc.nparts, seg_cap, cp, &ok);
+                        pc.nparts, seg_cap, rp, &ok);
                     if (!ok) {
                         if (lane == 0) defer_row(sm, row, out_ids, out_status);
                     } else {
-                        finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, n, cp, row,
+                        finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, n, rp, row,
                                     out_ids, out_status, out_probs);
                     }
                     if (lane == 0) row_arrivals[row] = 0;  // ready for the next call
@@ -1359,7 +1379,8 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                void *seg_records, uint32_t *row_arrivals, uint32_t *scratch,
                                uint32_t slots, uint32_t *slot_lock, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
-    cudaError_t e = prepare(stream_topk_kernel<false>, sizeof(StreamSmem));
+    auto kernel = p.row_params ? stream_topk_kernel<false, true> : stream_topk_kernel<false, false>;
+    cudaError_t e = prepare(kernel, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid, 1, 1);
@@ -1371,7 +1392,7 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, stream_topk_kernel<false>, logits, rows, vocab, row_stride, p,
+    return cudaLaunchKernelEx(&cfg, kernel, logits, rows, vocab, row_stride, p,
                               out_ids, out_status, out_probs, scratch, slots, slot_lock, 0u,
                               static_cast<unsigned char *>(nullptr),
                               split_record_bytes(plan.max_parts), plan.nch, plan.streamk,

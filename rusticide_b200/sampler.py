@@ -205,6 +205,22 @@ class Engine:
               "rsc_sample")
         return ids, status, probs
 
+    def sample_rows(self, logits: torch.Tensor, params: Sequence[SamplingParams],
+                    uniforms: Optional[torch.Tensor] = None,
+                    rng_states: Optional[torch.Tensor] = None, want_probs: bool = True, out=None):
+        """rsc_sample_rows: row r is Sampler::sample_logits(row r, params[r]).
+        Returns (ids, status, probs)."""
+        rows, vocab, stride = self._check_rows(logits)
+        if len(params) != rows:
+            raise SamplingError(f"InvalidShape: {len(params)} parameter sets for {rows} rows")
+        ids, status, probs = out if out is not None else self._outputs(rows, want_probs)
+        arr = (_lib.RscParams * max(1, rows))(*[p.to_c() for p in params])
+        check(self.lib.rsc_sample_rows(self._h, logits.data_ptr(), rows, vocab, stride, arr,
+                                       _ptr(uniforms), _ptr(rng_states), ids.data_ptr(),
+                                       status.data_ptr(), _ptr(probs), _stream_ptr(self.device)),
+              "rsc_sample_rows")
+        return ids, status, probs
+
     def sample_ex(self, logits: torch.Tensor, params: SamplingParams,
                   uniforms: Optional[torch.Tensor] = None,
                   rng_states: Optional[torch.Tensor] = None, survivor_cap: int = 0):
