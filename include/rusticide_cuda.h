@@ -139,11 +139,16 @@ RSC_API rsc_status rsc_sample_rows(rsc_sampler *sampler, const float *d_logits, 
  * d_n_survivors   uint32 per row, nullable: size of the set.
  * d_survivor_ids  rows x survivor_cap uint32, nullable: the first
  *                 min(n, survivor_cap) token ids of the set.
+ * d_survivor_probs rows x survivor_cap f32, nullable: the probabilities of
+ *                 the same survivors, the vector the reference's softmax
+ *                 returns for the row (src/filters.rs:5-15, as
+ *                 src/sampler.rs:50 computes it); entry i belongs to id i.
  */
 typedef struct {
     uint32_t *d_n_survivors;
     uint32_t *d_survivor_ids;
     size_t survivor_cap;
+    float *d_survivor_probs;
 } rsc_sample_extras;
 
 /* rsc_sample with optional extra outputs (extras may be NULL). */

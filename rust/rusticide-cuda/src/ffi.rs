@@ -37,6 +37,7 @@ pub(crate) struct RscSampleExtras {
     pub(crate) d_n_survivors: *mut u32,
     pub(crate) d_survivor_ids: *mut u32,
     pub(crate) survivor_cap: usize,
+    pub(crate) d_survivor_probs: *mut f32,
 }
 
 /// Opaque `rsc_sampler`.

@@ -54,6 +54,7 @@ class RscSampleExtras(ctypes.Structure):
         ("d_n_survivors", ctypes.c_void_p),
         ("d_survivor_ids", ctypes.c_void_p),
         ("survivor_cap", ctypes.c_size_t),
+        ("d_survivor_probs", ctypes.c_void_p),
     ]
 
 

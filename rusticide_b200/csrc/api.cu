@@ -113,6 +113,7 @@ rsc::CallParams rows_from(const rsc::CallParams &cp, size_t r0) {
     if (b.rng_states) b.rng_states += r0;
     if (b.out_nsurv) b.out_nsurv += r0;
     if (b.out_surv) b.out_surv += r0 * b.surv_cap;
+    if (b.out_survp) b.out_survp += r0 * b.surv_cap;
     if (b.row_params) b.row_params += r0;
     return b;
 }
@@ -285,10 +286,12 @@ rsc_status rsc_sample_ex(rsc_sampler *s, const float *d_logits, size_t rows, siz
     rsc::CallParams cp = make_params(*params, vocab, d_uniforms, d_rng_states);
     if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
     if (extras) {
-        if (extras->d_survivor_ids && (extras->survivor_cap == 0 || extras->survivor_cap > 0xffffffffull))
+        if ((extras->d_survivor_ids || extras->d_survivor_probs) &&
+            (extras->survivor_cap == 0 || extras->survivor_cap > 0xffffffffull))
             return RSC_ERR_INVALID_ARGUMENT;
         cp.out_nsurv = extras->d_n_survivors;
         cp.out_surv = extras->d_survivor_ids;
+        cp.out_survp = extras->d_survivor_probs;
         cp.surv_cap = static_cast<uint32_t>(extras->survivor_cap);
     }
     DeviceGuard guard(s->device);

@@ -198,6 +198,7 @@ struct CallParams {
     uint32_t *out_nsurv;     // nullable: survivor count per row
     uint32_t *out_surv;      // nullable: rows x surv_cap survivor ids
     uint32_t surv_cap;
+    float *out_survp = nullptr;   // nullable: rows x surv_cap survivor probabilities
     const rsc_params *row_params = nullptr;  // one parameter set per row (rsc_sample_rows)
 };
 

@@ -435,8 +435,21 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
     last = block_reduce<T>(last, sm.red32, OpMaxU32());
     any = block_reduce<T>(any, sm.red32, OpOrU32());
 
-    // Optional survivor outputs (count, and the first surv_cap ids in order).
-    if (cp.out_nsurv || cp.out_surv) {
+    // --- softmax sum (filters.rs:7-8) -----------------------------------------------
+    const double *tab = sm.exp_tab;
+    auto row_value = [&](uint32_t i) { return rv.value(i); };
+    float sum = -0.0f;
+    if (any) {
+        auto s_term = exp_term(row_value, survivor, mx, 1.0f, false, tab);
+        sum = block_replay<T, kReplayItems>(n, s_term, [](float) { return false; }, sm.rs).sum;
+    }
+    const bool norm = (fabsf(sum) < kPosInf) && sum > 0.0f;
+
+    // Optional survivor outputs: the count, and the first surv_cap ids in
+    // index order with their probabilities (the softmax vector of
+    // filters.rs:5-15: exp(v - max), divided by the sum when it is finite
+    // and positive).
+    if (cp.out_nsurv || cp.out_surv || cp.out_survp) {
         uint32_t written = 0;
         constexpr uint32_t kTile = T * kItems;
         for (uint32_t t0 = 0; t0 < n; t0 += kTile) {
@@ -450,12 +463,19 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
             }
             uint32_t total;
             uint32_t off = block_exclusive_add<T>(cnt, sm.red32, &total);
-            if (cp.out_surv) {
+            if (cp.out_surv || cp.out_survp) {
 #pragma unroll
                 for (int q = 0; q < kItems; ++q) {
                     if (keep[q]) {
-                        if (written + off < cp.surv_cap)
-                            cp.out_surv[row * cp.surv_cap + written + off] = t0 + threadIdx.x * kItems + q;
+                        const uint32_t i = t0 + threadIdx.x * kItems + q;
+                        if (written + off < cp.surv_cap) {
+                            const size_t at = row * cp.surv_cap + written + off;
+                            if (cp.out_surv) cp.out_surv[at] = i;
+                            if (cp.out_survp) {
+                                const float e = expf_ref(__fsub_rn(rv.value(i), mx), tab);
+                                cp.out_survp[at] = norm ? __fdiv_rn(e, sum) : e;
+                            }
+                        }
                         ++off;
                     }
                 }
@@ -465,16 +485,6 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
         if (cp.out_nsurv && threadIdx.x == 0) cp.out_nsurv[row] = written;
         __syncthreads();
     }
-
-    // --- softmax sum (filters.rs:7-8) -----------------------------------------------
-    const double *tab = sm.exp_tab;
-    auto row_value = [&](uint32_t i) { return rv.value(i); };
-    float sum = -0.0f;
-    if (any) {
-        auto s_term = exp_term(row_value, survivor, mx, 1.0f, false, tab);
-        sum = block_replay<T, kReplayItems>(n, s_term, [](float) { return false; }, sm.rs).sum;
-    }
-    const bool norm = (fabsf(sum) < kPosInf) && sum > 0.0f;
 
     // valid_probabilities (sampler.rs:133-139): some survivor has p > 0 and
     // is not NaN. exp and the division are monotone, so with a finite
@@ -535,7 +545,7 @@ __device__ void sample_row(const CallParams &cp, const float *p, uint32_t vocab,
                            uint32_t *scratch, uint32_t *out_ids, int32_t *out_status,
                            float *out_probs, LargeSmem<T> &sm) {
     RowView rv{p, vocab, cp.scale, cp.mode == kModeSampleWithTemp};
-    const bool plain = !cp.out_nsurv && !cp.out_surv &&
+    const bool plain = !cp.out_nsurv && !cp.out_surv && !cp.out_survp &&
                        (rv.with_temp || (cp.normal_scale && !cp.topk_active && !cp.topp_active));
     if (plain) plain_row<T>(cp, rv, row, out_ids, out_status, out_probs, sm);
     else large_row<T>(cp, rv, row, scratch, out_ids, out_status, out_probs, sm);

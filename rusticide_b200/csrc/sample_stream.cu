@@ -524,6 +524,10 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
     }
     valid = __any_sync(0xffffffffu, valid);
     __syncwarp();
+    if (cp.out_survp) {
+        const uint32_t m = min(n, cp.surv_cap);
+        for (uint32_t i = lane; i < m; i += 32) cp.out_survp[row * cp.surv_cap + i] = fw.vals[i];
+    }
     if (lane == 0) {
         int32_t status = RSC_ROW_NO_VALID_TOKENS;
         uint32_t token = 0;

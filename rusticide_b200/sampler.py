@@ -224,21 +224,24 @@ class Engine:
     def sample_ex(self, logits: torch.Tensor, params: SamplingParams,
                   uniforms: Optional[torch.Tensor] = None,
                   rng_states: Optional[torch.Tensor] = None, survivor_cap: int = 0):
-        """rsc_sample_ex: rsc_sample plus each row's surviving candidate set.
-        Returns (ids, status, probs, n_survivors, survivor_ids[rows, cap])."""
+        """rsc_sample_ex: rsc_sample plus each row's surviving candidate set and
+        its probabilities. Returns (ids, status, probs, n_survivors,
+        survivor_ids[rows, cap], survivor_probs[rows, cap])."""
         rows, vocab, stride = self._check_rows(logits)
         ids, status, probs = self._outputs(rows, True)
         nsurv = torch.empty(rows, dtype=torch.int32, device=self.device)
         cap = max(1, int(survivor_cap))
         surv = torch.full((rows, cap), -1, dtype=torch.int32, device=self.device)
+        survp = torch.full((rows, cap), float("nan"), dtype=torch.float32, device=self.device)
         ex = _lib.RscSampleExtras(nsurv.data_ptr(), surv.data_ptr() if survivor_cap else None,
-                                  cap if survivor_cap else 0)
+                                  cap if survivor_cap else 0,
+                                  survp.data_ptr() if survivor_cap else None)
         c = params.to_c()
         check(self.lib.rsc_sample_ex(self._h, logits.data_ptr(), rows, vocab, stride,
                                      ctypes.byref(c), _ptr(uniforms), _ptr(rng_states),
                                      ids.data_ptr(), status.data_ptr(), _ptr(probs),
                                      ctypes.byref(ex), _stream_ptr(self.device)), "rsc_sample_ex")
-        return ids, status, probs, nsurv, surv
+        return ids, status, probs, nsurv, surv, survp
 
     def pick(self, logits: torch.Tensor, params: SamplingParams,
              uniforms: Optional[torch.Tensor] = None, rng_states: Optional[torch.Tensor] = None,

@@ -62,7 +62,7 @@ class GpuBackend:
         t, k, p = params
         x2 = dev(np.asarray(x, dtype=np.float32).reshape(1, -1))
         n = max(1, x2.shape[1])
-        _, _, _, ns, surv = self.e.sample_ex(x2, SamplingParams(t, k, p),
+        _, _, _, ns, surv, _ = self.e.sample_ex(x2, SamplingParams(t, k, p),
                                              uniforms=dev(np.array([0.5])), survivor_cap=n)
         m = int(ns[0])
         return surv[0, :m].cpu().numpy(), None
@@ -112,12 +112,13 @@ def compare(eng, x: np.ndarray, params: SamplingParams, u: np.ndarray, tag: str,
     """Runs the engine and the oracle on the same rows; asserts parity."""
     rows, vocab = x.shape
     cap = vocab if check_surv else 0
-    ids, st, probs, ns, surv = eng.sample_ex(dev(x), params, uniforms=dev(u), survivor_cap=cap)
+    ids, st, probs, ns, surv, survp = eng.sample_ex(dev(x), params, uniforms=dev(u), survivor_cap=cap)
     ids = ids.cpu().numpy().view(np.uint32)
     st = st.cpu().numpy()
     probs = probs.cpu().numpy()
     ns = ns.cpu().numpy()
     surv = surv.cpu().numpy()
+    survp = survp.cpu().numpy()
     op = O.params(params.temperature, params.top_k, params.top_p)
     want = O.sample_rows(x, op, u, threads=8)
     stats = {"rows": rows, "edge": 0}
@@ -135,9 +136,17 @@ def compare(eng, x: np.ndarray, params: SamplingParams, u: np.ndarray, tag: str,
         if int(st[r]) & 0x100:
             stats["edge"] += 1
         if check_surv:
-            idx, _ = O.filter_(x[r], op)
+            idx, vals = O.filter_(x[r], op)
             assert ns[r] == len(idx), f"{tag} row {r}: {ns[r]} survivors != {len(idx)}"
             assert np.array_equal(surv[r, :len(idx)].view(np.uint32), idx), f"{tag} row {r}: survivor ids"
+            # The survivors' probabilities: the reference's softmax vector, bit
+            # for bit (any NaN matches any NaN: x86 and CUDA differ in the sign
+            # and payload of the NaNs they create).
+            got_p, want_p = survp[r, :len(idx)], O.softmax(vals)
+            nan = np.isnan(want_p)
+            assert np.array_equal(np.isnan(got_p), nan), f"{tag} row {r}: survivor prob NaNs"
+            assert np.array_equal(got_p[~nan].view(np.uint32), want_p[~nan].view(np.uint32)), \
+                f"{tag} row {r}: survivor probs"
     return stats
 
 
@@ -260,7 +269,7 @@ def test_headline_full_size(eng):
     x.scatter_add_(1, spikes, 5.0 + 7.0 * torch.rand(cfg.rows, 25, device="cuda", generator=g))
     u = torch.rand(cfg.rows, device="cuda", generator=g)
     params = SamplingParams(cfg.temperature, cfg.top_k, cfg.top_p)
-    ids, st, probs, ns, _ = eng.sample_ex(x, params, uniforms=u)
+    ids, st, probs, ns, _, _ = eng.sample_ex(x, params, uniforms=u)
     st_h = st.cpu().numpy()
     assert np.all(st_h & 0xFF == 0)
     # Property: the chosen token is among the row's top-40 scaled logits.
