@@ -531,7 +531,7 @@ rsc_status check_lmhead(const rsc_sampler *s, const void *d_hidden, const void *
 // call of the handle.
 rsc_status ensure_lm_records(rsc_sampler *s) {
     if (s->lm_records) return RSC_OK;
-    // Part records, then the group records of each reduction level.
+    // One record per vocabulary part and row.
     const size_t bytes = static_cast<size_t>(rsc::kLmheadRecordSlots) * s->max_rows *
                          rsc::shard_record_bytes(rsc::kLmheadRowCap - RSC_SHARD_TIE_CAP);
     if (cudaMalloc(&s->lm_records, bytes) != cudaSuccess) return RSC_ERR_CUDA;
@@ -587,23 +587,10 @@ rsc_status rsc_lmhead_sample(rsc_sampler *s, const void *d_hidden, const void *d
                                        nullptr, s->lm_records, rec_bytes, parts, s->lm_error, strm);
     ++s->launches;
     if (e != cudaSuccess) return RSC_ERR_CUDA;
-    // One merge list holds the records of kSmallCap / (k + 24) parts; more
-    // parts are first reduced, level by level, in groups of that many.
-    const uint32_t group = rsc::kSmallCap / (params->top_k + RSC_SHARD_TIE_CAP);
-    const unsigned char *cur = static_cast<const unsigned char *>(s->lm_records);
-    unsigned char *next = static_cast<unsigned char *>(s->lm_records) +
-                          static_cast<size_t>(parts) * rows * rec_bytes;
-    size_t n = parts;
-    while (n > group) {
-        e = rsc::launch_shard_reduce(cur, n, rows, rec_bytes, group, cp, next, strm);
-        ++s->launches;
-        if (e != cudaSuccess) return RSC_ERR_CUDA;
-        n = (n + group - 1) / group;
-        cur = next;
-        next += n * rows * rec_bytes;
-    }
-    e = rsc::launch_shard_merge(cur, n, rows, rec_bytes, cp, d_out_ids, d_out_status, d_out_probs,
-                                s->num_sms, strm);
+    // One block per row merges all parts' records (at most 256 parts of at
+    // most 64 entries).
+    e = rsc::launch_shard_merge_block(s->lm_records, parts, rows, rec_bytes, cp, d_out_ids,
+                                      d_out_status, d_out_probs, strm);
     ++s->launches;
     return cuda_status(e);
 }

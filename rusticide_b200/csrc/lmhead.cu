@@ -161,7 +161,8 @@ __host__ __device__ inline PartSpan part_span(uint32_t vocab, uint32_t part, uin
 // count at the floor is within k + slack. Returns the floor; n becomes the
 // number of entries kept, in place and in list order.
 __device__ __forceinline__ uint32_t warp_cut_row(uint32_t *lkey, uint16_t *lidx, uint32_t rr,
-                                                 uint32_t &n, uint32_t k, uint32_t slack) {
+                                                 uint32_t &n, uint32_t k, uint32_t slack,
+                                                 uint32_t KS = kKeyStride, uint32_t IS = kIdxStride) {
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t key[3];
     uint16_t idx[3];
@@ -169,8 +170,8 @@ __device__ __forceinline__ uint32_t warp_cut_row(uint32_t *lkey, uint16_t *lidx,
     for (int i = 0; i < 3; ++i) {
         const uint32_t e = lane + 32u * i;
         // Key 0 is a negative NaN pattern: never a candidate, never counted.
-        key[i] = e < n ? lkey[e * kKeyStride + rr] : 0u;
-        idx[i] = e < n ? lidx[e * kIdxStride + rr] : static_cast<uint16_t>(0);
+        key[i] = e < n ? lkey[e * KS + rr] : 0u;
+        idx[i] = e < n ? lidx[e * IS + rr] : static_cast<uint16_t>(0);
     }
     uint32_t floor_key = 0;
     for (int bit = 31; bit >= 0; --bit) {
@@ -194,8 +195,8 @@ __device__ __forceinline__ uint32_t warp_cut_row(uint32_t *lkey, uint16_t *lidx,
         const uint32_t ball = __ballot_sync(0xffffffffu, keep);
         if (keep) {
             const uint32_t pos = base + __popc(ball & lt);
-            lkey[pos * kKeyStride + rr] = key[i];
-            lidx[pos * kIdxStride + rr] = idx[i];
+            lkey[pos * KS + rr] = key[i];
+            lidx[pos * IS + rr] = idx[i];
         }
         base += __popc(ball);
     }
@@ -505,6 +506,379 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
     if (threadIdx.x == 0 && sm.error) atomicExch(error_out, 1u);
 }
 
+// --- decode-sized batches: operands swapped --------------------------------
+//
+// For rows <= kSN the tensor cores compute the transposed product: A is a
+// tile of up to 128 vocabulary rows of W, B the whole batch of hidden states
+// (N = rows rounded up to 16), so that an accumulator holds 128 vocabulary
+// entries (lanes) by the batch (columns). A stage then carries 16 KiB of W
+// and at most 8 KiB of H, and 6 (64 rows) to 11 (16 rows) stages stream the
+// weights. The epilogue
+// transposes each tile through shared memory, and warp e of the epilogue
+// owns the batch rows b = e (mod 4): it filters the tile's 128 values of its
+// rows (4 per lane, ballot appends) into the rows' lists, with the same cuts
+// and records as the row-tile kernel.
+constexpr int kSN = 64;                       // batch rows of the swapped path (MMA N <= 64)
+constexpr uint32_t kSMaxStages = 16;
+constexpr uint32_t kSTmemCols = 2 * kSN;
+constexpr uint32_t kSWStage = kBM * kBK * sizeof(__nv_bfloat16);  // 16 KiB of W per stage
+constexpr uint32_t kMaxDynSmem = 232448;                           // 227 KiB per CTA
+constexpr uint32_t kSAtoms = 2;                                    // 64-column k atoms per stage
+
+// Row state and barriers, after the ring and the buffers.
+struct SmallHead {
+    float rtau[kSN];  // per batch row: bound, count, overflow, max key
+    uint32_t rcnt[kSN];
+    uint32_t rovf[kSN];
+    uint32_t rmaxkey[kSN];
+    uint64_t full[kSMaxStages];
+    uint64_t empty[kSMaxStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint32_t tmem_base;
+    uint32_t error;
+};
+
+// Shared memory of the swapped path, sized for the batch (n_pad rows): nst
+// ring stages of W (16 KiB) and H (n_pad x 128 B), the tile transpose
+// [n_pad][128] f32, the lists with slot strides n_pad + 1 (keys) and
+// n_pad + 2 (indices: odd word strides keep a row's slots in distinct banks),
+// then the head. Everything a batch does not use goes to more stages: the
+// weights in flight per SM bound this kernel.
+struct SmallLayout {
+    uint32_t nst, apb, wb, hb, ks, is;
+    uint32_t off_h, off_tb, off_key, off_idx, off_head, bytes;
+};
+// apb: 64-column k atoms per stage, so that a stage reads apb * 128
+// contiguous bytes of each weight row.
+__host__ __device__ inline SmallLayout small_layout(uint32_t n_pad, uint32_t nst, uint32_t apb) {
+    SmallLayout L;
+    L.nst = nst;
+    L.apb = apb;
+    L.wb = apb * kSWStage;
+    L.hb = apb * n_pad * kBK * static_cast<uint32_t>(sizeof(__nv_bfloat16));
+    L.ks = n_pad + 1;
+    L.is = n_pad + 2;
+    L.off_h = nst * L.wb;
+    L.off_tb = L.off_h + nst * L.hb;
+    L.off_key = L.off_tb + n_pad * kBM * 4u;
+    L.off_idx = L.off_key + kListCap * L.ks * 4u;
+    L.off_head = (L.off_idx + kListCap * L.is * 2u + 15u) & ~15u;
+    L.bytes = L.off_head + static_cast<uint32_t>(sizeof(SmallHead)) + 1024u;  // + alignment slack
+    return L;
+}
+// The most stages that fit (at least 2).
+inline uint32_t small_stages(uint32_t n_pad, uint32_t apb) {
+    uint32_t nst = kSMaxStages;
+    while (nst > 2 && small_layout(n_pad, nst, apb).bytes > kMaxDynSmem) --nst;
+    return nst;
+}
+
+// Tile t of a part's span in the swapped path: full 128-column tiles from
+// the part's start, the last one narrower. (Splitting a part evenly into
+// tiles of 112 and 128 columns made most tiles narrow; a narrow tile's
+// 16-row boxes stream at two thirds of the rate of full boxes.)
+__device__ __forceinline__ void small_tile(const PartSpan &sp, uint32_t t, uint32_t &c, uint32_t &w) {
+    c = sp.c0 + t * kBM;
+    w = min(static_cast<uint32_t>(kBM), sp.cend - c);
+}
+__host__ __device__ inline uint32_t small_tiles(const PartSpan &sp) {
+    const uint32_t units = (sp.cend - sp.c0) / kUnit;
+    return (units + kBM / kUnit - 1) / (kBM / kUnit);
+}
+
+// Named barrier 1 over the 128 epilogue threads, plain and with an OR vote.
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool epi_bar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 1, 128, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"(v ? 1u : 0u)
+        : "memory");
+    return r != 0u;
+}
+
+template <bool kFused>
+__global__ void __launch_bounds__(kGThreads, 1)
+lmhead_small_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
+                    const __grid_constant__ CUtensorMap map_w16, uint32_t rows, uint32_t n_pad,
+                    uint32_t nst, uint32_t apb, uint32_t dim, uint32_t vocab, CallParams cp,
+                    float *__restrict__ logits, unsigned char *__restrict__ records,
+                    size_t rec_bytes, uint32_t *__restrict__ error_out) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *base = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+    const SmallLayout lay = small_layout(n_pad, nst, apb);
+    SmallHead &sm = *reinterpret_cast<SmallHead *>(base + lay.off_head);
+    float *tb = reinterpret_cast<float *>(base + lay.off_tb);
+    uint32_t *lkey = reinterpret_cast<uint32_t *>(base + lay.off_key);
+    uint16_t *lidx = reinterpret_cast<uint16_t *>(base + lay.off_idx);
+    const uint32_t ks = lay.ks, is = lay.is;
+    auto wst = [&](uint32_t s) { return reinterpret_cast<__nv_bfloat16 *>(base + s * lay.wb); };
+    auto hst = [&](uint32_t s) { return reinterpret_cast<__nv_bfloat16 *>(base + lay.off_h + s * lay.hb); };
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t part = blockIdx.x, parts = gridDim.x;
+    PartSpan span = part_span(vocab, part, parts);
+    span.ntiles = small_tiles(span);
+    const uint32_t kblocks = (dim + kBK * apb - 1) / (kBK * apb);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < nst; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sm.acc_full[b], 1);
+            mbar_init(&sm.acc_empty[b], kBM / 32);
+        }
+        sm.error = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(&sm.tmem_base)),
+                     "r"(kSTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+    volatile uint32_t *err = &sm.error;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            const uint32_t hbytes = n_pad * kBK * static_cast<uint32_t>(sizeof(__nv_bfloat16));
+            for (uint32_t t = 0; t < span.ntiles && ok; ++t) {
+                uint32_t c, w;
+                small_tile(span, t, c, w);
+                for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
+                    const uint32_t s = it % nst;
+                    if (it >= nst && !mbar_wait(&sm.empty[s], ((it / nst) - 1u) & 1u)) {
+                        *err = 1u;
+                        ok = false;
+                        break;
+                    }
+                    if (*err) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&sm.full[s], apb * (hbytes + w * kBK * static_cast<uint32_t>(
+                                                                                  sizeof(__nv_bfloat16))));
+                    for (uint32_t a = 0; a < apb; ++a) {
+                        // Atoms past dim read zeros (out-of-range boxes).
+                        const int32_t x = static_cast<int32_t>((kb * apb + a) * kBK);
+                        __nv_bfloat16 *wa = wst(s) + a * kBM * kBK;
+                        tma_load_2d(hst(s) + a * n_pad * kBK, &map_h, &sm.full[s], x, 0);
+                        if (w == static_cast<uint32_t>(kBM)) {
+                            tma_load_2d(wa, &map_w, &sm.full[s], x, static_cast<int32_t>(c));
+                        } else {
+                            for (uint32_t i = 0; i < w / kUnit; ++i)
+                                tma_load_2d(wa + i * kUnit * kBK, &map_w16, &sm.full[s], x,
+                                            static_cast<int32_t>(c + i * kUnit));
+                        }
+                    }
+                }
+            }
+            const uint32_t first = it > nst ? it - nst : 0u;
+            for (uint32_t i = first; i < it; ++i) mbar_wait(&sm.full[i % nst], (i / nst) & 1u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            const uint32_t idesc = idesc_for(n_pad);
+            for (uint32_t t = 0; t < span.ntiles && ok; ++t) {
+                const uint32_t buf = t & 1u;
+                if (t >= 2 && !mbar_wait(&sm.acc_empty[buf], ((t >> 1) - 1u) & 1u)) {
+                    *err = 1u;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + buf * kSN;
+                for (uint32_t kb = 0; kb < kblocks; ++kb, ++it) {
+                    const uint32_t s = it % nst;
+                    if (!mbar_wait(&sm.full[s], (it / nst) & 1u) || *err) {
+                        *err = 1u;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (uint32_t a = 0; a < apb; ++a) {
+                        const uint32_t sa = smem_addr(wst(s) + a * kBM * kBK);
+                        const uint32_t sb = smem_addr(hst(s) + a * n_pad * kBK);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / kUK; ++kk) {
+                            const uint32_t off = static_cast<uint32_t>(kk * kUK * sizeof(__nv_bfloat16));
+                            mma_bf16(d, smem_desc(sa + off), smem_desc(sb + off), idesc,
+                                     (kb | a | static_cast<uint32_t>(kk)) ? 1u : 0u);
+                        }
+                    }
+                    mma_commit(&sm.empty[s]);
+                }
+                if (ok) mma_commit(&sm.acc_full[buf]);
+            }
+            if (it > 0) mbar_wait(&sm.empty[(it - 1) % nst], ((it - 1) / nst) & 1u);
+        }
+    } else {
+        // Epilogue: thread (warp, lane) reads tensor-memory lane 32 * (warp % 4)
+        // + lane, vocabulary row v of the tile, for every batch row.
+        const uint32_t q = static_cast<uint32_t>(warp) & 3u;
+        const uint32_t ew = static_cast<uint32_t>(warp) - 2u;  // owns batch rows ew + 4j
+        const uint32_t v = 32u * q + lane;
+        const float scale = cp.scale;
+        const uint32_t k = cp.top_k;
+        if (kFused) {
+            for (uint32_t b = ew; b < static_cast<uint32_t>(kSN); b += 4u) {
+                if (lane == 0) {
+                    sm.rtau[b] = -3.402823466e38f;
+                    sm.rcnt[b] = 0;
+                    sm.rovf[b] = 0;
+                    sm.rmaxkey[b] = total_key(kNegInf);
+                }
+            }
+            __syncwarp();
+        }
+        for (uint32_t t = 0; t < span.ntiles; ++t) {
+            const uint32_t buf = t & 1u;
+            uint32_t c, w;
+            small_tile(span, t, c, w);
+            const uint32_t col = c + v;
+            const bool valid = v < w && col < vocab;
+            const bool got = mbar_wait(&sm.acc_full[buf], (t >> 1) & 1u);
+            // The fused epilogue's warps meet at named barriers, so they give
+            // up together (a vote) or not at all.
+            const bool bad = kFused ? epi_bar_or(!got || *err != 0u)
+                                    : __any_sync(0xffffffffu, !got) || *err != 0u;
+            if (bad) {
+                if (lane == 0) *err = 1u;
+                break;
+            }
+            tc_fence_after();
+            if (!kFused) {
+                for (uint32_t cb = 0; cb < n_pad; cb += 16) {
+                    uint32_t r16[16];
+                    tmem_ld16(tmem + buf * kSN + cb + ((32u * q) << 16), r16);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const uint32_t b = cb + j;
+                        if (valid && b < rows) logits[static_cast<size_t>(b) * vocab + col] = __uint_as_float(r16[j]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+            } else {
+            for (uint32_t cb = 0; cb < n_pad; cb += 16) {
+                uint32_t r16[16];
+                tmem_ld16(tmem + buf * kSN + cb + ((32u * q) << 16), r16);
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    tb[(cb + j) * kBM + v] = valid ? scale_logit(__uint_as_float(r16[j]), scale) : kNegInf;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+            epi_bar();  // the tile's values are in tb
+            const uint32_t steps = (w + 31u) / 32u;
+            for (uint32_t b = ew; b < rows; b += 4u) {
+                if (sm.rovf[b]) continue;
+                float tau = sm.rtau[b];
+                uint32_t cnt = sm.rcnt[b];
+                bool ovf = false;
+                float lmax = kNegInf;
+                for (uint32_t i = 0; i < steps; ++i) {
+                    if (cnt > kListCap - 32u) {
+                        uint32_t n = cnt;
+                        const uint32_t fk = warp_cut_row(lkey, lidx, b, n, k, kFloorSlack, ks, is);
+                        cnt = n;
+                        const float f = key_to_float(fk);
+                        if (f > tau) tau = f;
+                        if (cnt > kListCap - 32u) {
+                            // More ties at the k-th value than the list holds.
+                            ovf = true;
+                            break;
+                        }
+                    }
+                    const uint32_t vi = lane + 32u * i;
+                    const float x = tb[b * kBM + vi];
+                    lmax = fmaxf(lmax, x);
+                    const bool take = x >= tau;
+                    const uint32_t ball = __ballot_sync(0xffffffffu, take);
+                    if (take) {
+                        const uint32_t pos = cnt + __popc(ball & ((1u << lane) - 1u));
+                        lkey[pos * ks + b] = total_key(x);
+                        lidx[pos * is + b] = static_cast<uint16_t>(c + vi - span.c0);
+                    }
+                    cnt += __popc(ball);
+                    __syncwarp();
+                }
+                const uint32_t mk = __reduce_max_sync(0xffffffffu, total_key(lmax));
+                if (lane == 0) {
+                    sm.rtau[b] = tau;
+                    sm.rcnt[b] = cnt;
+                    sm.rovf[b] = ovf ? 1u : 0u;
+                    if (mk > sm.rmaxkey[b]) sm.rmaxkey[b] = mk;
+                }
+                __syncwarp();
+            }
+            epi_bar();  // tb is free for the next tile
+            }
+        }
+        if (kFused) {
+            const uint32_t cap = k + RSC_SHARD_TIE_CAP;
+            for (uint32_t b = ew; b < rows; b += 4u) {
+                uint32_t n = sm.rcnt[b];
+                bool o = sm.rovf[b] != 0u;
+                float rt = sm.rtau[b];
+                if (!o && n > cap) {
+                    const uint32_t fk = warp_cut_row(lkey, lidx, b, n, k, kFloorSlack, ks, is);
+                    const float f = key_to_float(fk);
+                    if (f > rt) rt = f;
+                    if (n > cap) o = true;
+                }
+                unsigned char *rec = records + (static_cast<size_t>(part) * rows + b) * rec_bytes;
+                ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                uint32_t *rkey = reinterpret_cast<uint32_t *>(rec + sizeof(ShardRecordHeader));
+                uint32_t *ridx = rkey + cap;
+                const uint32_t nw = o ? 0u : n;
+                for (uint32_t e = lane; e < nw; e += 32u) {
+                    rkey[e] = lkey[e * ks + b];
+                    ridx[e] = span.c0 + lidx[e * is + b];
+                }
+                if (lane == 0) {
+                    h->max_scaled = key_to_float(sm.rmaxkey[b]);
+                    h->sum_exp = 0.0f;
+                    h->n_finite = 0;
+                    h->n_cand = nw;
+                    h->n_dropped = 0;
+                    h->last_key = 0;
+                    h->flags = (o || *err) ? 1u : 0u;
+                    h->tau = o ? -3.402823466e38f : rt;
+                }
+                __syncwarp();
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kSTmemCols)
+                     : "memory");
+    }
+    if (threadIdx.x == 0 && sm.error) atomicExch(error_out, 1u);
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // dependency on the driver library).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -541,8 +915,13 @@ bool make_map(CUtensorMap *map, const void *base, uint64_t outer, uint64_t dim, 
 
 uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms) {
     const size_t mtiles = (rows + kBM - 1) / kBM;
-    const uint32_t ntiles = (vocab + kBN - 1) / kBN;
-    size_t p = mtiles ? static_cast<size_t>(num_sms) / mtiles : 1;
+    // Swapped operands (rows <= kSN): one part per SM, tiles of 128 columns;
+    // row tiles otherwise: the SMs shared among the row tiles.
+    const uint32_t ntiles = rows <= static_cast<size_t>(kSN) ? (vocab + kBM - 1) / kBM
+                                                              : (vocab + kBN - 1) / kBN;
+    size_t p = rows <= static_cast<size_t>(kSN) ? static_cast<size_t>(num_sms)
+               : mtiles                         ? static_cast<size_t>(num_sms) / mtiles
+                                                : 1;
     if (p < 1) p = 1;
     if (p > ntiles) p = ntiles;
     // Candidate indices are kept relative to the part's first column in 16
@@ -562,6 +941,38 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
     if ((static_cast<uint64_t>(vocab) + kUnit - 1) / kUnit > static_cast<uint64_t>(parts) * 4096u)
         return cudaErrorInvalidValue;  // a part would span more than 65536 columns
     CUtensorMap mh, mw, mw16;
+    if (rows <= static_cast<size_t>(kSN)) {
+        const uint32_t n_pad = static_cast<uint32_t>((rows + 15) / 16 * 16);
+        // Two k atoms per stage: 256 contiguous bytes of each weight row. One
+        // atom streamed the weights at 4.7 TB/s, two at 6.1 TB/s (1 row);
+        // four fit only 2 stages and gained nothing.
+        const uint32_t apb = kSAtoms;
+        if (small_layout(n_pad, 2, apb).bytes > kMaxDynSmem) return cudaErrorInvalidValue;
+        const uint32_t nst = small_stages(n_pad, apb);
+        const uint32_t smem = small_layout(n_pad, nst, apb).bytes;
+        if (!make_map(&mh, hidden, rows, dim, n_pad) || !make_map(&mw, weight, vocab, dim, kBM) ||
+            !make_map(&mw16, weight, vocab, dim, kUnit))
+            return cudaErrorInvalidValue;
+        const dim3 grid(parts, 1, 1);
+        if (logits) {
+            cudaError_t e = cudaFuncSetAttribute(lmhead_small_kernel<false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kMaxDynSmem));
+            if (e != cudaSuccess) return e;
+            lmhead_small_kernel<false><<<grid, kGThreads, smem, stream>>>(
+                mh, mw, mw16, static_cast<uint32_t>(rows), n_pad, nst, apb, dim, vocab, p, logits, nullptr,
+                0, error_flag);
+        } else {
+            cudaError_t e = cudaFuncSetAttribute(lmhead_small_kernel<true>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kMaxDynSmem));
+            if (e != cudaSuccess) return e;
+            lmhead_small_kernel<true><<<grid, kGThreads, smem, stream>>>(
+                mh, mw, mw16, static_cast<uint32_t>(rows), n_pad, nst, apb, dim, vocab, p, nullptr,
+                static_cast<unsigned char *>(records), rec_bytes, error_flag);
+        }
+        return cudaGetLastError();
+    }
     if (!make_map(&mh, hidden, rows, dim, kBM) || !make_map(&mw, weight, vocab, dim, kBN) ||
         !make_map(&mw16, weight, vocab, dim, kUnit))
         return cudaErrorInvalidValue;

@@ -74,12 +74,11 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
 // record of a row holds at most kLmheadRowCap candidates, so top_k <=
 // kLmheadRowCap - RSC_SHARD_TIE_CAP; a row is spread over at most
 // kLmheadMaxParts parts of at most 65536 columns each (vocab <=
-// kLmheadMaxVocab), whose records are reduced in groups until one merge list
-// holds them.
+// kLmheadMaxVocab), whose records one block per row merges.
 constexpr uint32_t kLmheadRowCap = 64;
 constexpr uint32_t kLmheadMaxParts = 256;
 constexpr uint64_t kLmheadMaxVocab = uint64_t{kLmheadMaxParts} * 65536u;
-constexpr uint32_t kLmheadRecordSlots = kLmheadMaxParts + 48;  // parts + reduction levels
+constexpr uint32_t kLmheadRecordSlots = kLmheadMaxParts;  // one record per part and row
 uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms);
 // logits != nullptr: writes rows x vocab f32 logits; otherwise writes one
 // shard record per (part, row) into records ([parts][rows], rec_bytes each).
@@ -115,14 +114,17 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
                                  void *records, size_t rec_bytes, int num_sms,
                                  cudaStream_t stream);
 
-// Merges the part records [n_parts][rows] in groups of `group` (at most
-// kSmallCap / (k + RSC_SHARD_TIE_CAP) parts) into group records
-// [ceil(n_parts / group)][rows] of the same format.
-cudaError_t launch_shard_reduce(const void *records, size_t n_parts, size_t rows, size_t rec_bytes,
-                                uint32_t group, const CallParams &p, void *out, cudaStream_t stream);
 cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows, size_t rec_bytes,
                                const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                                float *out_probs, int num_sms, cudaStream_t stream);
+// One block per row over all n_parts records (records of k + RSC_SHARD_TIE_CAP
+// entries, [n_parts][rows]): the merge of launch_shard_merge in one step for
+// up to 256 parts of at most 64 entries (shared memory
+// shard_merge_block_smem bytes).
+size_t shard_merge_block_smem(uint32_t n_parts, uint32_t cap_entries);
+cudaError_t launch_shard_merge_block(const void *records, size_t n_parts, size_t rows,
+                                     size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
+                                     int32_t *out_status, float *out_probs, cudaStream_t stream);
 
 cudaError_t launch_penalize(float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                             const uint32_t *tokens, size_t n_tokens, float penalty,

@@ -1262,45 +1262,170 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
     }
 }
 
-// Two-level merge for rows spread over more parts than one candidate list can
-// take: each warp merges up to kReduceGroup part records of one row into one
-// record of the same format (the group's candidates at or above the largest
-// of its parts' bounds, capped at k + RSC_SHARD_TIE_CAP like a part record).
-__global__ void __launch_bounds__(kMergeWarps * 32)
-shard_reduce_kernel(const unsigned char *__restrict__ records, size_t n_parts, size_t rows,
-                    size_t rec_bytes, uint32_t group, CallParams cp,
-                    unsigned char *__restrict__ out) {
+// One block per row: the records of up to kLmheadMaxParts parts of a row in
+// one pass, for rows spread over more parts than a warp's candidate list can
+// merge (the LM-head epilogue's 148 and more). Two lower bounds of the row's
+// k-th largest value cut the union before it is read: the largest of the
+// parts' own bounds, and the k-th largest of the parts' maxima (k distinct
+// values, each the top of its part). Only parts whose maximum reaches the
+// bound are read; their entries at or above it go to shared memory, where
+// the block selects the row's k-th largest key (radix select), keeps the
+// entries at or above it (ties included) and finishes the row with one warp
+// exactly as the streaming kernel does: the result of the warp merge
+// (shard_merge_kernel) over the same records, for any number of parts.
+constexpr int kBlockMergeThreads = 512;
+
+struct BlockMergeSmem {
+    CandList list;
+    FinishWork fw;
+    double exp_tab[32];
+    uint32_t hist[256];
+    uint32_t sel[2];
+    float redf[kBlockMergeThreads / 32];
+    uint32_t red32[kBlockMergeThreads / 32];
+    uint32_t count, kept, nsel;
+    float bound;
+    uint32_t ncand[kLmheadMaxParts];  // entries of each part
+    float pmax[kLmheadMaxParts];      // each part's largest scaled logit
+    uint32_t psel[kLmheadMaxParts];   // the parts that can hold candidates
+    // then uint32 key[entries], uint32 idx[entries]
+};
+
+__global__ void __launch_bounds__(kBlockMergeThreads)
+shard_merge_block_kernel(const unsigned char *__restrict__ records, uint32_t n_parts, size_t rows,
+                         size_t rec_bytes, uint32_t cap_entries, CallParams cp,
+                         uint32_t *__restrict__ out_ids, int32_t *__restrict__ out_status,
+                         float *__restrict__ out_probs) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    MergeSmem &sm = *reinterpret_cast<MergeSmem *>(smem_raw);
+    BlockMergeSmem &sm = *reinterpret_cast<BlockMergeSmem *>(smem_raw);
+    const uint32_t entries = n_parts * cap_entries;
+    uint32_t *bkey = reinterpret_cast<uint32_t *>(smem_raw + sizeof(BlockMergeSmem));
+    uint32_t *bidx = bkey + entries;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    CandList &L = sm.list[warp];
-    FinishWork &fw = sm.fw[warp];
-    const size_t n_groups = (n_parts + group - 1) / group;
-    const uint32_t cap = cp.top_k + RSC_SHARD_TIE_CAP;
-    for (size_t w = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; w < n_groups * rows;
-         w += static_cast<size_t>(gridDim.x) * kMergeWarps) {
-        const size_t g = w / rows, row = w % rows;
-        const size_t p0 = g * group;
-        const uint32_t n = static_cast<uint32_t>(min(static_cast<size_t>(group), n_parts - p0));
-        bool ok = true;
-        float tau = 0.0f;
-        const uint32_t count = merge_records(
-            L, fw, [&](uint32_t part) { return records + ((p0 + part) * rows + row) * rec_bytes; },
-            n, cap, cp, &ok, &tau);
-        unsigned char *rec = out + (g * rows + row) * rec_bytes;
-        if (!ok) {
-            if (lane == 0) {
-                ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
-                h->n_cand = 0;
-                h->n_dropped = 0;
-                h->flags = 1;
+    const size_t row = blockIdx.x;
+    auto rec_at = [&](uint32_t part) { return records + (static_cast<size_t>(part) * rows + row) * rec_bytes; };
+    load_exp_table(sm.exp_tab);
+    if (threadIdx.x == 0) {
+        sm.count = 0;
+        sm.kept = 0;
+        sm.nsel = 0;
+        sm.bound = kNegInf;
+    }
+    // Headers: the parts' flags and bounds.
+    uint32_t bad = 0, dropped = 0;
+    float tau = -3.402823466e38f;
+    for (uint32_t p = threadIdx.x; p < n_parts; p += kBlockMergeThreads) {
+        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(p));
+        if (__ldcg(h + 6) != 0u) bad = 1u;
+        if (__ldcg(h + 4) != 0u) dropped = 1u;
+        tau = fmaxf(tau, __uint_as_float(__ldcg(h + 7)));
+        sm.ncand[p] = min(__ldcg(h + 3), cap_entries);
+        sm.pmax[p] = __uint_as_float(__ldcg(h + 0));
+    }
+    tau = block_reduce<kBlockMergeThreads>(tau, sm.redf, OpFMax());
+    bad = block_reduce<kBlockMergeThreads>(bad, sm.red32, OpOrU32());
+    dropped = block_reduce<kBlockMergeThreads>(dropped, sm.red32, OpOrU32());
+    // The k-th largest part maximum (by value, then part): the part whose
+    // maximum has exactly k - 1 parts before it.
+    if (cp.topk_active && n_parts >= cp.top_k) {
+        for (uint32_t p = threadIdx.x; p < n_parts; p += kBlockMergeThreads) {
+            const float m = sm.pmax[p];
+            uint32_t rank = 0;
+            for (uint32_t q = 0; q < n_parts; ++q) {
+                const float o = sm.pmax[q];
+                rank += (o > m || (o == m && q < p)) ? 1u : 0u;
             }
-            __syncwarp();
-            continue;
+            if (rank == cp.top_k - 1u) sm.bound = m;
         }
-        record_list(fw, L.key, L.idx, count, cp, 0.0f, 0.0f, 0u, rec, cap, tau);
+    }
+    __syncthreads();
+    tau = fmaxf(tau, sm.bound);
+    // The parts whose maximum reaches the bound.
+    for (uint32_t p = threadIdx.x; p < n_parts; p += kBlockMergeThreads)
+        if (sm.pmax[p] >= tau) sm.psel[atomicAdd(&sm.nsel, 1u)] = p;
+    __syncthreads();
+    const uint32_t slots = sm.nsel * cap_entries;
+    // Entries at or above the bound. Entry e of selected part j is flat slot
+    // j * cap + e; each thread loads kGather slots at once, so that the loads
+    // overlap.
+    constexpr uint32_t kGather = 8;
+    if (!bad) {
+        for (uint32_t base = 0; base < slots; base += kBlockMergeThreads * kGather) {
+            uint32_t key[kGather], idx[kGather];
+#pragma unroll
+            for (uint32_t q = 0; q < kGather; ++q) {
+                const uint32_t f = base + q * kBlockMergeThreads + threadIdx.x;
+                const uint32_t j = f / cap_entries, e = f - j * cap_entries;
+                const uint32_t p = f < slots ? sm.psel[j] : 0u;
+                const bool valid = f < slots && e < sm.ncand[p];
+                const uint32_t *rkey = reinterpret_cast<const uint32_t *>(rec_at(p)) + 8;
+                key[q] = valid ? __ldcg(rkey + e) : 0u;
+                idx[q] = valid ? __ldcg(rkey + cap_entries + e) : 0u;
+                if (!valid) key[q] = 0u;  // key 0 (a NaN pattern) is never kept
+            }
+#pragma unroll
+            for (uint32_t q = 0; q < kGather; ++q) {
+                const bool keep = key[q] != 0u && key_to_float(key[q]) >= tau;
+                const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+                uint32_t at = 0;
+                if (lane == 0 && ballot) at = atomicAdd(&sm.count, static_cast<uint32_t>(__popc(ballot)));
+                at = __shfl_sync(0xffffffffu, at, 0);
+                if (keep) {
+                    const uint32_t pos = at + __popc(ballot & ((1u << lane) - 1u));
+                    bkey[pos] = key[q];
+                    bidx[pos] = idx[q];
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t count = sm.count;  // <= entries: each part gives at most cap_entries
+    uint32_t floor_key = 0u;
+    const bool have_kth = !bad && cp.topk_active && count >= cp.top_k;
+    if (have_kth) {
+        const uint32_t kth = block_select_kth_largest<kBlockMergeThreads>(
+            count, cp.top_k, [&](uint32_t i) { return bkey[i]; }, sm.hist, sm.sel);
+        floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
+    }
+    // A part that dropped tied entries that can reach the row's k-th value
+    // leaves the union incomplete.
+    if (!bad && dropped) {
+        uint32_t b = 0;
+        for (uint32_t p = threadIdx.x; p < n_parts; p += kBlockMergeThreads) {
+            const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(p));
+            if (__ldcg(h + 4) > 0 && (!have_kth || __ldcg(h + 5) >= floor_key)) b = 1u;
+        }
+        bad = block_reduce<kBlockMergeThreads>(b, sm.red32, OpOrU32());
+    }
+    // The row's candidates: the entries at or above the k-th (all of them
+    // without top-k), into the finisher's list.
+    if (!bad) {
+        for (uint32_t i = threadIdx.x; i < count; i += kBlockMergeThreads) {
+            if (bkey[i] >= floor_key) {
+                const uint32_t pos = atomicAdd(&sm.kept, 1u);
+                if (pos < kCap) {
+                    sm.list.key[pos] = bkey[i];
+                    sm.list.idx[pos] = bidx[i];
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t kept = sm.kept;
+    if (warp == 0) {
+        if (bad || kept > kCap) {
+            if (lane == 0) {
+                out_ids[row] = 0;
+                out_status[row] = RSC_ROW_INTERNAL;
+                if (out_probs) out_probs[row] = __uint_as_float(0x7fc00000u);
+            }
+        } else {
+            finish_list(sm.fw, sm.exp_tab, sm.list.key, sm.list.idx, kept, cp, row, out_ids,
+                        out_status, out_probs);
+        }
     }
 }
+
 
 template <typename K>
 cudaError_t prepare(K kernel, size_t smem) {
@@ -1421,16 +1546,24 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
     return cudaGetLastError();
 }
 
-cudaError_t launch_shard_reduce(const void *records, size_t n_parts, size_t rows, size_t rec_bytes,
-                                uint32_t group, const CallParams &p, void *out, cudaStream_t stream) {
-    if (rows == 0 || n_parts == 0) return cudaSuccess;
-    cudaError_t e = prepare(shard_reduce_kernel, sizeof(MergeSmem));
+size_t shard_merge_block_smem(uint32_t n_parts, uint32_t cap_entries) {
+    return sizeof(BlockMergeSmem) + static_cast<size_t>(n_parts) * cap_entries * 8u;
+}
+
+cudaError_t launch_shard_merge_block(const void *records, size_t n_parts, size_t rows,
+                                     size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
+                                     int32_t *out_status, float *out_probs, cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    const uint32_t cap = p.top_k + RSC_SHARD_TIE_CAP;
+    const size_t smem = shard_merge_block_smem(static_cast<uint32_t>(n_parts), cap);
+    if (n_parts > kLmheadMaxParts || smem > 232448) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(shard_merge_block_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const size_t n_groups = (n_parts + group - 1) / group;
-    const size_t grid = (n_groups * rows + kMergeWarps - 1) / kMergeWarps;
-    shard_reduce_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem), stream>>>(
-        static_cast<const unsigned char *>(records), n_parts, rows, rec_bytes, group, p,
-        static_cast<unsigned char *>(out));
+    shard_merge_block_kernel<<<static_cast<unsigned>(rows), kBlockMergeThreads, smem, stream>>>(
+        static_cast<const unsigned char *>(records), static_cast<uint32_t>(n_parts), rows, rec_bytes,
+        cap, p, out_ids, out_status, out_probs);
     return cudaGetLastError();
 }
 

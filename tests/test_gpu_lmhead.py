@@ -19,8 +19,11 @@ from rusticide_b200.sampler import SamplingError
 pytestmark = pytest.mark.gpu
 
 # (rows, dim, vocab): partial row tiles, a dim that is not a multiple of 64,
-# partial vocab tiles, and a Qwen-sized vocab shard.
-SHAPES = [(1, 64, 300), (5, 256, 4096), (130, 1000, 5000), (64, 512, 18992)]
+# partial vocab tiles, and a Qwen-sized vocab shard. Up to 64 rows take the
+# swapped-operand kernel (batch padded to 16, 32, 48 or 64), more rows the
+# row-tile kernel.
+SHAPES = [(1, 64, 300), (5, 256, 4096), (17, 136, 777), (64, 512, 18992), (65, 256, 3000),
+          (130, 1000, 5000)]
 
 
 def _inputs(rows, dim, vocab, seed):
