@@ -5,7 +5,7 @@
 //! `sample_with_temp` would (crates/rusticide-sampling/src/sampler.rs:44-105),
 //! on an sm_100a GPU through `librusticide_cuda.so`.
 //!
-//! Two entry points:
+//! Three entry points:
 //!
 //! * [`CudaSampler::pick_rows`]: host rows in, tokens out, safe. It is the
 //!   batched form of `rusticide_model::generate::pick`
@@ -17,6 +17,8 @@
 //!   reference's token sequence for the same seed.
 //! * [`CudaSampler::sample_device`]: rows already in device memory (a GPU
 //!   model's LM head). `unsafe`: the caller vouches for the device pointers.
+//! * [`CudaSampler::sample_rows_device`]: the same with one `SamplingParams`
+//!   per row, for a batch of sequences that each carry their own parameters.
 //!
 //! `unsafe` in this crate is limited to the FFI calls; each block states why
 //! the call is sound.
