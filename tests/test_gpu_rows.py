@@ -119,3 +119,25 @@ def test_rows_reject_bad_arguments(eng):
     ids, st, _ = eng.sample_rows(x, [SamplingParams(0.0, 40, 0.9)] * 4)  # argmax rows need none
     torch.cuda.synchronize()
     assert (st & 0xFF).eq(0).all()
+
+
+def test_rows_beyond_one_launch():
+    """More rows than one streaming launch takes (148 SMs x 3 CTAs x 48 rows =
+    21312 on a B200): the call is split into launches, and each launch must
+    read the parameter sets of its own rows."""
+    from rusticide_b200.sampler import Engine
+    rows, vocab = 21412, 700
+    eng = Engine(0, rows, vocab)  # its own handle: small staging buffers
+    x = synth.make_logits(rows, vocab, base_seed=21)
+    u = synth.uniforms(rows, seed=22)
+    choice = _choice(rows, seed=23)
+    ps = [SamplingParams(*MIX[m]) for m in choice]
+    ids, st, pr = eng.sample_rows(dev(x), ps, uniforms=dev(u))
+    torch.cuda.synchronize()
+    for m, idx in _groups(choice):
+        ti = torch.from_numpy(idx).cuda()
+        gi, gs, gp = eng.sample(dev(x[idx]), SamplingParams(*MIX[m]), uniforms=dev(u[idx]))
+        assert torch.equal(ids[ti], gi), f"params {MIX[m]}"
+        assert torch.equal(st[ti] & 0x1FF, gs & 0x1FF)
+        assert torch.equal(pr[ti].view(torch.int32), gp.view(torch.int32))
+    eng.close()
