@@ -320,6 +320,24 @@ RSC_API rsc_status rsc_lmhead_sample(rsc_sampler *sampler, const void *d_hidden,
                                      int32_t *d_out_status, float *d_out_probs, void *stream);
 
 /*
+ * rsc_lmhead_sample for a tensor-parallel LM head: this GPU holds the
+ * vocabulary rows [shard_offset, shard_offset + shard_vocab) of W
+ * (d_weight_shard, shard_vocab x dim bf16) and the whole batch of hidden
+ * states. Writes one shard record per row to d_records (rows x
+ * rsc_shard_record_bytes(top_k) bytes), with global token ids, in the format
+ * of rsc_shard_partial: all-gather the ranks' records in rank order and call
+ * rsc_shard_merge with global_vocab, and every rank gets the tokens that
+ * rsc_lmhead_sample returns on the whole W. No counterpart in the reference,
+ * whose LM head runs on one host (crates/rusticide-transformer/src/
+ * decoder.rs:104-105). Parameter limits as rsc_lmhead_sample, with top-k
+ * judged against global_vocab.
+ */
+RSC_API rsc_status rsc_lmhead_partial(rsc_sampler *sampler, const void *d_hidden,
+                                      const void *d_weight_shard, size_t rows, size_t dim,
+                                      size_t shard_vocab, size_t shard_offset, size_t global_vocab,
+                                      const rsc_params *params, void *d_records, void *stream);
+
+/*
  * Evaluates the library's binary32 exp, the function the sampler applies to
  * v - max (Rust's f32::exp, i.e. glibc expf, src/filters.rs:7 and
  * src/candidates.rs:64), on n device floats: d_y[i] = exp(d_x[i]). Exposed so

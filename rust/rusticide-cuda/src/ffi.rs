@@ -230,6 +230,19 @@ unsafe extern "C" {
         d_out_probs: *mut f32,
         stream: *mut c_void,
     ) -> c_int;
+    pub(crate) fn rsc_lmhead_partial(
+        sampler: *mut RscSampler,
+        d_hidden: *const c_void,
+        d_weight_shard: *const c_void,
+        rows: usize,
+        dim: usize,
+        shard_vocab: usize,
+        shard_offset: usize,
+        global_vocab: usize,
+        params: *const RscParams,
+        d_records: *mut c_void,
+        stream: *mut c_void,
+    ) -> c_int;
     pub(crate) fn rsc_expf(d_x: *const f32, d_y: *mut f32, n: usize, stream: *mut c_void) -> c_int;
     pub(crate) fn rsc_launch_count(sampler: *const RscSampler) -> u64;
 }

@@ -84,6 +84,8 @@ SIGNATURES = {
     "rsc_sample_noalloc": (_ST, [_P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P,
                                  _P]),
     "rsc_lmhead_logits": (_ST, [_P, _P, _P, _SZ, _SZ, _SZ, _P, _P]),
+    "rsc_lmhead_partial": (_ST, [_P, _P, _P, _SZ, _SZ, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams),
+                                 _P, _P]),
     "rsc_lmhead_sample": (_ST, [_P, _P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P,
                                 _P, _P, _P]),
     "rsc_expf": (_ST, [_P, _P, _SZ, _P]),

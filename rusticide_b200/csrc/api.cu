@@ -595,6 +595,41 @@ rsc_status rsc_lmhead_sample(rsc_sampler *s, const void *d_hidden, const void *d
     return cuda_status(e);
 }
 
+rsc_status rsc_lmhead_partial(rsc_sampler *s, const void *d_hidden, const void *d_weight_shard,
+                              size_t rows, size_t dim, size_t shard_vocab, size_t shard_offset,
+                              size_t global_vocab, const rsc_params *params, void *d_records,
+                              void *stream) {
+    rsc_status st = check_lmhead(s, d_hidden, d_weight_shard, rows, dim, shard_vocab);
+    if (st != RSC_OK) return st;
+    if (!params) return RSC_ERR_INVALID_ARGUMENT;
+    if (global_vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (shard_offset > global_vocab || shard_vocab > global_vocab - shard_offset)
+        return RSC_ERR_INVALID_SHAPE;
+    if (rows == 0) return RSC_OK;
+    if (!d_records) return RSC_ERR_INVALID_ARGUMENT;
+    // The global vocabulary decides whether top-k is on, as for the whole row.
+    const rsc::CallParams cp = make_params(*params, global_vocab, nullptr, nullptr);
+    if (!cp.topk_active || !cp.normal_scale ||
+        params->top_k + RSC_SHARD_TIE_CAP > rsc::kLmheadRowCap)
+        return RSC_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(s->device);
+    st = ensure_lm_records(s);
+    if (st != RSC_OK) return st;
+    const uint32_t v = static_cast<uint32_t>(shard_vocab);
+    const uint32_t parts = rsc::lmhead_parts(rows, v, s->num_sms);
+    const size_t rec_bytes = rsc::shard_record_bytes(params->top_k);
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    cudaError_t e = rsc::launch_lmhead(d_hidden, d_weight_shard, rows, static_cast<uint32_t>(dim), v,
+                                       cp, nullptr, s->lm_records, rec_bytes, parts, s->lm_error,
+                                       strm, static_cast<uint32_t>(shard_offset));
+    ++s->launches;
+    if (e != cudaSuccess) return RSC_ERR_CUDA;
+    // The shard's parts reduced to one record per row.
+    e = rsc::launch_shard_reduce_block(s->lm_records, parts, rows, rec_bytes, cp, d_records, strm);
+    ++s->launches;
+    return cuda_status(e);
+}
+
 rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream) {
     if (n == 0) return RSC_OK;
     if (!d_x || !d_y) return RSC_ERR_INVALID_ARGUMENT;

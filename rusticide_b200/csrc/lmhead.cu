@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
 lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
               const __grid_constant__ CUtensorMap map_w16, uint32_t rows, uint32_t dim,
               uint32_t vocab, CallParams cp, float *__restrict__ logits, bool vec_out,
-              unsigned char *__restrict__ records, size_t rec_bytes,
+              unsigned char *__restrict__ records, size_t rec_bytes, uint32_t index_offset,
               uint32_t *__restrict__ error_out) {
     extern __shared__ unsigned char smem_raw[];
     LmSmem &sm = *reinterpret_cast<LmSmem *>(
@@ -478,7 +478,7 @@ lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__
                 const uint32_t nw = o ? 0u : n;
                 for (uint32_t e = lane; e < nw; e += 32u) {
                     rkey[e] = sm.lkey[e * kKeyStride + rr];
-                    ridx[e] = span.c0 + sm.lidx[e * kIdxStride + rr];
+                    ridx[e] = index_offset + span.c0 + sm.lidx[e * kIdxStride + rr];
                 }
                 if (lane == 0) {
                     h->max_scaled = rmax;
@@ -608,7 +608,7 @@ lmhead_small_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_cons
                     const __grid_constant__ CUtensorMap map_w16, uint32_t rows, uint32_t n_pad,
                     uint32_t nst, uint32_t apb, uint32_t dim, uint32_t vocab, CallParams cp,
                     float *__restrict__ logits, unsigned char *__restrict__ records,
-                    size_t rec_bytes, uint32_t *__restrict__ error_out) {
+                    size_t rec_bytes, uint32_t index_offset, uint32_t *__restrict__ error_out) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char *base = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
@@ -851,7 +851,7 @@ lmhead_small_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_cons
                 const uint32_t nw = o ? 0u : n;
                 for (uint32_t e = lane; e < nw; e += 32u) {
                     rkey[e] = lkey[e * ks + b];
-                    ridx[e] = span.c0 + lidx[e * is + b];
+                    ridx[e] = index_offset + span.c0 + lidx[e * is + b];
                 }
                 if (lane == 0) {
                     h->max_scaled = key_to_float(sm.rmaxkey[b]);
@@ -936,7 +936,7 @@ uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms) {
 cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, uint32_t dim,
                           uint32_t vocab, const CallParams &p, float *logits, void *records,
                           size_t rec_bytes, uint32_t parts, uint32_t *error_flag,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, uint32_t index_offset) {
     if (rows == 0) return cudaSuccess;
     if ((static_cast<uint64_t>(vocab) + kUnit - 1) / kUnit > static_cast<uint64_t>(parts) * 4096u)
         return cudaErrorInvalidValue;  // a part would span more than 65536 columns
@@ -961,7 +961,7 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
             if (e != cudaSuccess) return e;
             lmhead_small_kernel<false><<<grid, kGThreads, smem, stream>>>(
                 mh, mw, mw16, static_cast<uint32_t>(rows), n_pad, nst, apb, dim, vocab, p, logits, nullptr,
-                0, error_flag);
+                0, index_offset, error_flag);
         } else {
             cudaError_t e = cudaFuncSetAttribute(lmhead_small_kernel<true>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -969,7 +969,7 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
             if (e != cudaSuccess) return e;
             lmhead_small_kernel<true><<<grid, kGThreads, smem, stream>>>(
                 mh, mw, mw16, static_cast<uint32_t>(rows), n_pad, nst, apb, dim, vocab, p, nullptr,
-                static_cast<unsigned char *>(records), rec_bytes, error_flag);
+                static_cast<unsigned char *>(records), rec_bytes, index_offset, error_flag);
         }
         return cudaGetLastError();
     }
@@ -985,7 +985,7 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
         const bool vec = vocab % 4 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
         lmhead_kernel<false><<<grid, kGThreads, kLmSmemBytes, stream>>>(
             mh, mw, mw16, static_cast<uint32_t>(rows), dim, vocab, p, logits, vec, nullptr, 0,
-            error_flag);
+            index_offset, error_flag);
     } else {
         cudaError_t e = cudaFuncSetAttribute(lmhead_kernel<true>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -993,7 +993,7 @@ cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, u
         if (e != cudaSuccess) return e;
         lmhead_kernel<true><<<grid, kGThreads, kLmSmemBytes, stream>>>(
             mh, mw, mw16, static_cast<uint32_t>(rows), dim, vocab, p, nullptr, false,
-            static_cast<unsigned char *>(records), rec_bytes, error_flag);
+            static_cast<unsigned char *>(records), rec_bytes, index_offset, error_flag);
     }
     return cudaGetLastError();
 }

@@ -82,10 +82,12 @@ constexpr uint32_t kLmheadRecordSlots = kLmheadMaxParts;  // one record per part
 uint32_t lmhead_parts(size_t rows, uint32_t vocab, int num_sms);
 // logits != nullptr: writes rows x vocab f32 logits; otherwise writes one
 // shard record per (part, row) into records ([parts][rows], rec_bytes each).
+// index_offset: added to every record index (the vocabulary offset of a
+// weight shard).
 cudaError_t launch_lmhead(const void *hidden, const void *weight, size_t rows, uint32_t dim,
                           uint32_t vocab, const CallParams &p, float *logits, void *records,
                           size_t rec_bytes, uint32_t parts, uint32_t *error_flag,
-                          cudaStream_t stream);
+                          cudaStream_t stream, uint32_t index_offset = 0);
 
 // Vocab-sharded record: this header, then uint32 key[k + RSC_SHARD_TIE_CAP]
 // and uint32 index[k + RSC_SHARD_TIE_CAP] (global indices), entries sorted by
@@ -125,6 +127,12 @@ size_t shard_merge_block_smem(uint32_t n_parts, uint32_t cap_entries);
 cudaError_t launch_shard_merge_block(const void *records, size_t n_parts, size_t rows,
                                      size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
                                      int32_t *out_status, float *out_probs, cudaStream_t stream);
+// The same merge, writing one record per row of the same format into
+// out_records ([rows], rec_bytes each) instead of sampling: the parts of one
+// vocabulary shard reduced to the shard's record.
+cudaError_t launch_shard_reduce_block(const void *records, size_t n_parts, size_t rows,
+                                      size_t rec_bytes, const CallParams &p, void *out_records,
+                                      cudaStream_t stream);
 
 cudaError_t launch_penalize(float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                             const uint32_t *tokens, size_t n_tokens, float penalty,

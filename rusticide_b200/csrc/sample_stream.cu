@@ -1291,11 +1291,14 @@ struct BlockMergeSmem {
     // then uint32 key[entries], uint32 idx[entries]
 };
 
+// kEmit: instead of sampling the row, write its record (the parts reduced to
+// one part) to out_records.
+template <bool kEmit>
 __global__ void __launch_bounds__(kBlockMergeThreads)
 shard_merge_block_kernel(const unsigned char *__restrict__ records, uint32_t n_parts, size_t rows,
                          size_t rec_bytes, uint32_t cap_entries, CallParams cp,
                          uint32_t *__restrict__ out_ids, int32_t *__restrict__ out_status,
-                         float *__restrict__ out_probs) {
+                         float *__restrict__ out_probs, unsigned char *__restrict__ out_records) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     BlockMergeSmem &sm = *reinterpret_cast<BlockMergeSmem *>(smem_raw);
     const uint32_t entries = n_parts * cap_entries;
@@ -1323,6 +1326,9 @@ shard_merge_block_kernel(const unsigned char *__restrict__ records, uint32_t n_p
         sm.pmax[p] = __uint_as_float(__ldcg(h + 0));
     }
     tau = block_reduce<kBlockMergeThreads>(tau, sm.redf, OpFMax());
+    float rmax = kNegInf;  // the row's largest scaled logit over the parts
+    for (uint32_t p = threadIdx.x; p < n_parts; p += kBlockMergeThreads) rmax = fmaxf(rmax, sm.pmax[p]);
+    rmax = block_reduce<kBlockMergeThreads>(rmax, sm.redf, OpFMax());
     bad = block_reduce<kBlockMergeThreads>(bad, sm.red32, OpOrU32());
     dropped = block_reduce<kBlockMergeThreads>(dropped, sm.red32, OpOrU32());
     // The k-th largest part maximum (by value, then part): the part whose
@@ -1412,6 +1418,30 @@ shard_merge_block_kernel(const unsigned char *__restrict__ records, uint32_t n_p
     }
     __syncthreads();
     const uint32_t kept = sm.kept;
+    if (kEmit) {
+        if (warp == 0) {
+            unsigned char *rec = out_records + row * rec_bytes;
+            if (bad || kept > kCap) {
+                if (lane == 0) {
+                    ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                    h->max_scaled = rmax;
+                    h->sum_exp = 0.0f;
+                    h->n_finite = 0;
+                    h->n_cand = 0;
+                    h->n_dropped = 0;
+                    h->last_key = 0;
+                    h->flags = 1;
+                    h->tau = -3.402823466e38f;
+                }
+            } else {
+                // Entries at or above the row's k-th value (or, without a
+                // k-th, every candidate at or above the precut bound).
+                record_list(sm.fw, sm.list.key, sm.list.idx, kept, cp, rmax, 0.0f, 0u, rec,
+                            cap_entries, have_kth ? key_to_float(floor_key) : tau);
+            }
+        }
+        return;
+    }
     if (warp == 0) {
         if (bad || kept > kCap) {
             if (lane == 0) {
@@ -1557,13 +1587,30 @@ cudaError_t launch_shard_merge_block(const void *records, size_t n_parts, size_t
     const uint32_t cap = p.top_k + RSC_SHARD_TIE_CAP;
     const size_t smem = shard_merge_block_smem(static_cast<uint32_t>(n_parts), cap);
     if (n_parts > kLmheadMaxParts || smem > 232448) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(shard_merge_block_kernel,
+    cudaError_t e = cudaFuncSetAttribute(shard_merge_block_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    shard_merge_block_kernel<<<static_cast<unsigned>(rows), kBlockMergeThreads, smem, stream>>>(
+    shard_merge_block_kernel<false><<<static_cast<unsigned>(rows), kBlockMergeThreads, smem, stream>>>(
         static_cast<const unsigned char *>(records), static_cast<uint32_t>(n_parts), rows, rec_bytes,
-        cap, p, out_ids, out_status, out_probs);
+        cap, p, out_ids, out_status, out_probs, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shard_reduce_block(const void *records, size_t n_parts, size_t rows,
+                                      size_t rec_bytes, const CallParams &p, void *out_records,
+                                      cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    const uint32_t cap = p.top_k + RSC_SHARD_TIE_CAP;
+    const size_t smem = shard_merge_block_smem(static_cast<uint32_t>(n_parts), cap);
+    if (n_parts > kLmheadMaxParts || smem > 232448) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(shard_merge_block_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    shard_merge_block_kernel<true><<<static_cast<unsigned>(rows), kBlockMergeThreads, smem, stream>>>(
+        static_cast<const unsigned char *>(records), static_cast<uint32_t>(n_parts), rows, rec_bytes,
+        cap, p, nullptr, nullptr, nullptr, static_cast<unsigned char *>(out_records));
     return cudaGetLastError();
 }
 

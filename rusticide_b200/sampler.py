@@ -377,6 +377,25 @@ class Engine:
                                          _stream_ptr(self.device)), "rsc_lmhead_sample")
         return ids, status, probs
 
+    def lmhead_partial(self, hidden: torch.Tensor, weight_shard: torch.Tensor, shard_offset: int,
+                       global_vocab: int, params: SamplingParams,
+                       records: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """rsc_lmhead_partial: this rank's shard record per row for a
+        vocabulary shard of the LM head (rows [shard_offset, shard_offset +
+        weight_shard.shape[0]) of W), to all-gather and pass to shard_merge."""
+        hidden, weight_shard = self._lmhead_args(hidden, weight_shard)
+        rows, dim = hidden.shape
+        self.ensure(rows, 1)
+        rb = self.shard_record_bytes(params.top_k)
+        if records is None:
+            records = torch.empty(rows * rb, dtype=torch.uint8, device=self.device)
+        c = params.to_c()
+        check(self.lib.rsc_lmhead_partial(self._h, hidden.data_ptr(), weight_shard.data_ptr(), rows,
+                                          dim, weight_shard.shape[0], int(shard_offset),
+                                          int(global_vocab), ctypes.byref(c), records.data_ptr(),
+                                          _stream_ptr(self.device)), "rsc_lmhead_partial")
+        return records
+
 
 _ENGINES: dict[int, Engine] = {}
 

@@ -13,7 +13,10 @@ Two ways to spread a batch over GPUs:
   every rank merges the gathered records into the same token per row
   (rsc_shard_merge). Only records cross NVLink: rows x ranks x
   rsc_shard_record_bytes(k) bytes (544 B per row and rank at k = 40)
-  instead of the slices of the logits.
+  instead of the slices of the logits. `sample_lmhead` does the same for a
+  tensor-parallel LM head: each rank's slice of the weights goes through the
+  GEMM with the sampler in its epilogue (rsc_lmhead_partial), so the logits
+  are never written at all.
 
 The reference samples whole rows on one host (crates/rusticide-sampling/src/
 sampler.rs:44 sample_logits, :75 greedy_logits); sharding is this
@@ -87,6 +90,27 @@ class VocabShardedSampler:
         rows = logits_shard.shape[0]
         records, gathered = self._buffers(rows, params.top_k, logits_shard.device)
         self.engine.shard_partial(logits_shard, self.offset, self.vocab, params, records=records)
+        dist.all_gather_into_tensor(gathered, records, group=self.group)
+        return self.engine.shard_merge(gathered, self.world, rows, self.vocab, params,
+                                       uniforms=uniforms, rng_states=rng_states,
+                                       want_probs=want_probs, out=out)
+
+    def sample_lmhead(self, hidden: torch.Tensor, weight_shard: torch.Tensor, params,
+                      uniforms: Optional[torch.Tensor] = None,
+                      rng_states: Optional[torch.Tensor] = None, want_probs: bool = True,
+                      out=None):
+        """A tensor-parallel LM head with the sampler in its epilogue: this
+        rank holds the vocabulary rows [offset, offset + width) of W
+        (weight_shard, [width, dim] bf16) and every rank the same hidden
+        states [rows, dim]. The shard's logits never leave the GEMM
+        (rsc_lmhead_partial); only the shard records are all-gathered."""
+        if weight_shard.dim() != 2 or weight_shard.shape[0] != self.width:
+            raise ValueError(f"rank {self.rank} expects [{self.width}, dim] weights, "
+                             f"got {tuple(weight_shard.shape)}")
+        rows = hidden.shape[0]
+        records, gathered = self._buffers(rows, params.top_k, hidden.device)
+        self.engine.lmhead_partial(hidden, weight_shard, self.offset, self.vocab, params,
+                                   records=records)
         dist.all_gather_into_tensor(gathered, records, group=self.group)
         return self.engine.shard_merge(gathered, self.world, rows, self.vocab, params,
                                        uniforms=uniforms, rng_states=rng_states,

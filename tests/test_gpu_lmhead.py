@@ -107,3 +107,29 @@ def test_lmhead_tied_row_reports_internal(eng):
     assert torch.equal(st_f[keep], st_s[keep])
     assert torch.equal(ids_f[keep], ids_s[keep])
     assert torch.equal(pr_f[keep].view(torch.int32), pr_s[keep].view(torch.int32))
+
+
+@pytest.mark.parametrize("rows,dim,vocab,n_shards", [(1, 64, 300, 2), (5, 256, 4096, 2),
+                                                     (64, 512, 18992, 3), (130, 256, 5000, 4)])
+def test_lmhead_partial_shards_merge_to_the_fused_call(eng, rows, dim, vocab, n_shards):
+    """A tensor-parallel LM head emulated on one GPU: each vocabulary shard of W
+    through rsc_lmhead_partial, the records concatenated in shard order (what
+    the all-gather produces) and merged by rsc_shard_merge, must give the
+    tokens, statuses and probability bits of rsc_lmhead_sample on the whole W."""
+    from rusticide_b200.sharding import vocab_shard
+    h, w = _inputs(rows, dim, vocab, seed=rows * 3 + vocab)
+    params = SamplingParams(0.8, 40, 0.95)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    u = torch.rand(rows, device="cuda", generator=g)
+    recs = []
+    for r in range(n_shards):
+        off, width = vocab_shard(vocab, n_shards, r)
+        recs.append(eng.lmhead_partial(h, w[off:off + width], off, vocab, params).clone())
+    gathered = torch.cat(recs)
+    ids_m, st_m, pr_m = eng.shard_merge(gathered, n_shards, rows, vocab, params, uniforms=u)
+    ids_f, st_f, pr_f = eng.lmhead_sample(h, w, params, uniforms=u)
+    torch.cuda.synchronize()
+    assert torch.equal(st_m, st_f)
+    assert torch.equal(ids_m, ids_f)
+    assert torch.equal(pr_m.view(torch.int32), pr_f.view(torch.int32))
+    assert (st_m & 0xFF).eq(0).all()

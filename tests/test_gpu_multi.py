@@ -54,6 +54,86 @@ def _rank_main(rank, world, port, q):
         dist.destroy_process_group()
 
 
+LM_ROWS, LM_DIM, LM_VOCAB = 16, 1024, 32000
+
+
+def _lmhead_inputs():
+    """The same bf16 hidden states and LM-head weights on every rank (CPU
+    generator, then moved)."""
+    g = torch.Generator().manual_seed(2024)
+    h = torch.randn(LM_ROWS, LM_DIM, generator=g).bfloat16()
+    w = (torch.randn(LM_VOCAB, LM_DIM, generator=g) * (3.0 / LM_DIM ** 0.5)).bfloat16()
+    u = torch.rand(LM_ROWS, generator=g)
+    return h, w, u
+
+
+def _rank_lmhead(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    from rusticide_b200 import engine
+    from rusticide_b200.sharding import VocabShardedSampler
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        h, w, u = _lmhead_inputs()
+        vs = VocabShardedSampler(engine(rank), LM_VOCAB)
+        w_mine = w[vs.offset:vs.offset + vs.width].contiguous().to(dev)
+        ids, status, probs = vs.sample_lmhead(h.to(dev), w_mine, SamplingParams(0.8, 40, 0.95),
+                                              uniforms=u.to(dev))
+        torch.cuda.synchronize(dev)
+        q.put((rank, ids.cpu().numpy().tolist(), status.cpu().numpy().tolist(),
+               probs.cpu().numpy().view(np.uint32).tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_ranks(target, world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    while len(got) < world:
+        try:
+            rank, ids, st, pb = q.get(timeout=5)
+            got[rank] = (ids, st, pb)
+        except Exception:
+            if not all(p.is_alive() or p.exitcode == 0 for p in procs):
+                for p in procs:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail("a rank failed")
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return got
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tensor_parallel_lmhead_nccl_matches_fused_call():
+    """Each rank holds a vocabulary shard of the LM-head weights; the fused
+    GEMM + sampler per shard, an all-gather of the shard records and the merge
+    must give every rank the tokens of rsc_lmhead_sample on the whole W."""
+    from rusticide_b200 import engine
+    world = min(torch.cuda.device_count(), 4)
+    got = _run_ranks(_rank_lmhead, world)
+    h, w, u = _lmhead_inputs()
+    dev = torch.device("cuda", 0)
+    ids, st, pb = engine(0).lmhead_sample(h.to(dev), w.to(dev), SamplingParams(0.8, 40, 0.95),
+                                          uniforms=u.to(dev))
+    want = (ids.cpu().numpy().tolist(), st.cpu().numpy().tolist(),
+            pb.cpu().numpy().view(np.uint32).tolist())
+    for r in range(world):
+        assert got[r] == want, f"rank {r}"
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_vocab_sharded_nccl_matches_unsharded():
     from oracle import oracle as O

@@ -87,6 +87,15 @@ class _ColumnsEngine:
         return O.sample_rows(full, op, uniforms.numpy(), threads=1)
 
 
+class _LmheadColumnsEngine(_ColumnsEngine):
+    """Stand-in engine for the sharded LM head: the shard's logits are the f32
+    product of its weight rows with the hidden states, then a columns record."""
+
+    def lmhead_partial(self, hidden, weight_shard, offset, vocab, params, records):
+        logits = (hidden.float() @ weight_shard.float().T).contiguous()
+        return self.shard_partial(logits, offset, vocab, params, records)
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -133,6 +142,61 @@ def test_vocab_sharded_orchestration_matches_unsharded(world):
         assert p.exitcode == 0
     x = synth.make_logits(rows, vocab, base_seed=77)
     u = synth.uniforms(rows, seed=5)
+    ref = O.sample_rows(x, O.params(0.8, 40, 0.95), u, threads=1)
+    want = [(int(t), int(st)) for t, st in zip(ref["token"], ref["status"])]
+    for r in range(world):
+        assert got[r] == want, f"rank {r}"
+
+
+def _rank_lmhead_main(rank, world, port, rows, dim, vocab, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(9)
+        h = torch.randn(rows, dim, generator=g).bfloat16()
+        w = torch.randn(vocab, dim, generator=g).bfloat16()
+        u = torch.from_numpy(synth.uniforms(rows, seed=6))
+        eng = _LmheadColumnsEngine(max_width=vocab // world + vocab % world)
+        vs = VocabShardedSampler(eng, vocab)
+        with pytest.raises(ValueError):
+            vs.sample_lmhead(h, w, SamplingParams(0.8, 40, 0.95), uniforms=u)  # not a shard
+        res = vs.sample_lmhead(h, w[vs.offset:vs.offset + vs.width], SamplingParams(0.8, 40, 0.95),
+                               uniforms=u)
+        q.put((rank, [(int(t), int(st)) for t, st in zip(res["token"], res["status"])]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_lmhead_orchestration_matches_unsharded(world):
+    """VocabShardedSampler.sample_lmhead: each rank's weight rows, its global
+    offsets and the gathered order give the oracle's tokens on the whole
+    product (the device GEMM and records are covered by the GPU tests)."""
+    from oracle import oracle as O
+    rows, dim, vocab = 5, 16, 1001
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_lmhead_main, args=(r, world, port, rows, dim, vocab, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    while len(got) < world:
+        try:
+            rank, res = q.get(timeout=5)
+            got[rank] = res
+        except Exception:
+            assert all(p.is_alive() or p.exitcode == 0 for p in procs), "a rank failed"
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    g = torch.Generator().manual_seed(9)
+    h = torch.randn(rows, dim, generator=g).bfloat16()
+    w = torch.randn(vocab, dim, generator=g).bfloat16()
+    x = (h.float() @ w.float().T).numpy()
+    u = synth.uniforms(rows, seed=6)
     ref = O.sample_rows(x, O.params(0.8, 40, 0.95), u, threads=1)
     want = [(int(t), int(st)) for t, st in zip(ref["token"], ref["status"])]
     for r in range(world):
