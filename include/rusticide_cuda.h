@@ -249,7 +249,8 @@ RSC_API rsc_status rsc_shard_partial(rsc_sampler *sampler, const float *d_logits
  * rsc_sample on the unsharded row. Every rank that calls it with the same
  * gathered records and uniforms computes identical outputs. Rows whose shards
  * overflowed their record report RSC_ROW_INTERNAL and must be resampled
- * unsharded.
+ * unsharded. Up to 256 shards (RSC_ERR_CAPACITY beyond, or when the shards'
+ * records of one row exceed 227 KiB of shared memory).
  */
 RSC_API rsc_status rsc_shard_merge(rsc_sampler *sampler, const void *d_records,
                            size_t n_shards, size_t rows, size_t global_vocab,

@@ -499,15 +499,25 @@ rsc_status rsc_shard_merge(rsc_sampler *s, const void *d_records, size_t n_shard
     if (rows > 0 && (!d_records || !d_out_ids || !d_out_status)) return RSC_ERR_INVALID_ARGUMENT;
     rsc::CallParams cp = make_params(*params, global_vocab, d_uniforms, d_rng_states);
     if (!cp.topk_active || !cp.normal_scale) return RSC_ERR_INVALID_ARGUMENT;
-    if (n_shards * (static_cast<size_t>(params->top_k) + RSC_SHARD_TIE_CAP) > rsc::kSmallCap)
+    // One warp merges a row when the shards' records fit its candidate list;
+    // more shards (or a larger k) take one block per row, up to
+    // kLmheadMaxParts records whose union fits its shared memory.
+    const size_t cap = static_cast<size_t>(params->top_k) + RSC_SHARD_TIE_CAP;
+    const bool warp_merge = n_shards * cap <= rsc::kSmallCap;
+    if (!warp_merge && (n_shards > rsc::kLmheadMaxParts ||
+                        rsc::shard_merge_block_smem(static_cast<uint32_t>(n_shards),
+                                                    static_cast<uint32_t>(cap)) > 232448))
         return RSC_ERR_CAPACITY;
     if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
     if (rows == 0) return RSC_OK;
     DeviceGuard guard(s->device);
-    cudaError_t e = rsc::launch_shard_merge(d_records, n_shards, rows,
-                                            rsc::shard_record_bytes(params->top_k), cp, d_out_ids,
-                                            d_out_status, d_out_probs, s->num_sms,
-                                            static_cast<cudaStream_t>(stream));
+    const size_t rec_bytes = rsc::shard_record_bytes(params->top_k);
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    cudaError_t e = warp_merge
+                        ? rsc::launch_shard_merge(d_records, n_shards, rows, rec_bytes, cp, d_out_ids,
+                                                  d_out_status, d_out_probs, s->num_sms, strm)
+                        : rsc::launch_shard_merge_block(d_records, n_shards, rows, rec_bytes, cp,
+                                                        d_out_ids, d_out_status, d_out_probs, strm);
     ++s->launches;
     return cuda_status(e);
 }

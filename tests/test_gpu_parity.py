@@ -375,14 +375,17 @@ def test_pick_host_matches_device(eng):
 # ---------------------------------------------------------------------------
 # Vocab-sharded merge, emulated on one GPU (each shard a column slice)
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("n_shards", [2, 4, 8])
-def test_vocab_sharded_matches_unsharded(eng, n_shards):
+@pytest.mark.parametrize("n_shards,top_k", [(2, None), (4, None), (8, None), (10, 40), (16, 40)])
+def test_vocab_sharded_matches_unsharded(eng, n_shards, top_k):
+    """Shard records merged into the unsharded result. Up to n_shards * (k + 24)
+    = 512 entries per row one warp merges them; beyond (10 and 16 shards at
+    k 40) one block per row does."""
     cfg = synth.CONFIGS["cfg4"]
     rows = 16
     x = synth.make_config(cfg, rows=rows, base_seed=606)
     x[3, 100:140] = 9.0   # ties across a shard boundary
     u = synth.uniforms(rows, seed=13)
-    params = SamplingParams(cfg.temperature, cfg.top_k, cfg.top_p)
+    params = SamplingParams(cfg.temperature, top_k or cfg.top_k, cfg.top_p)
     xd = dev(x)
     V = cfg.vocab
     bounds = [V * s // n_shards for s in range(n_shards + 1)]
