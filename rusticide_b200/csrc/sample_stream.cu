@@ -96,6 +96,12 @@ struct StreamSmem {
 };
 static_assert(sizeof(large::LargeSmem<kThreads>) <= sizeof(float) * kStages * kChunk,
               "the epilogue's large-row workspace lives in the idle ring");
+// The epilogue's top-k histogram (4096 bins) sits in the idle ring after the
+// large-row workspace.
+constexpr uint32_t kTopkBins = 4096;
+constexpr size_t kTopkHistOffset = (sizeof(large::LargeSmem<kThreads>) + 255) & ~static_cast<size_t>(255);
+static_assert(kTopkHistOffset + kTopkBins * sizeof(uint32_t) <= sizeof(float) * kStages * kChunk,
+              "the top-k histogram fits the idle ring beside the large-row workspace");
 
 // Geometry of one row: a scalar head up to 16-byte alignment, a body of
 // `nbody` logits copied by TMA in chunks, a scalar tail.
@@ -785,6 +791,121 @@ __device__ __forceinline__ bool streams_row(const CallParams &r, uint32_t vocab)
            ((r.topk_active && r.top_k <= kSmallTopK) || (!r.topk_active && vocab <= kSmallCap));
 }
 
+// A deferred row with top-k on (its list overflowed, so its bound admitted
+// more than the list holds), by the whole CTA in two passes over the row:
+// a histogram of the top 12 bits of the candidates' keys finds the bin that
+// holds the k-th largest value; a second pass gathers every candidate at or
+// above that bin's smallest value into the finisher's list, which
+// finish_list completes exactly as for a streamed row (its list is any
+// superset of the survivors, all candidates at or above a bound no higher
+// than the k-th value). Returns false, with nothing written, when the row's
+// parameters are not the streaming filter's (top-k on, k <= kSmallTopK, a
+// normal scale) or the gather would exceed the list (heavy ties); the row
+// then takes the large-row code.
+__device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const float *p, uint32_t vocab,
+                                               size_t row, StreamSmem &sm, uint32_t *hist,
+                                               uint32_t *out_ids, int32_t *out_status,
+                                               float *out_probs) {
+    const CallParams cp = for_row(call, row, vocab);
+    if (!streams_row(cp, vocab) || !cp.topk_active) return false;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float scale = cp.scale;
+    for (uint32_t b = threadIdx.x; b < kTopkBins; b += kThreads) hist[b] = 0;
+    if (threadIdx.x == 0) sm.count[0] = 0;
+    __syncthreads();
+    // Candidates: every scaled value but -inf (NaN reads as -inf). Lanes of a
+    // warp that share a bin add once, through their leader. kGather loads per
+    // thread are in flight at once.
+    constexpr uint32_t kGather = 16;
+    for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
+        float x[kGather];
+#pragma unroll
+        for (uint32_t q = 0; q < kGather; ++q) {
+            const uint32_t i = base + q * kThreads + threadIdx.x;
+            x[q] = i < vocab ? p[i] : kNegInf;
+        }
+#pragma unroll
+        for (uint32_t q = 0; q < kGather; ++q) {
+            const float v = scale_logit(x[q], scale);
+            const uint32_t bin = v != kNegInf ? total_key(v) >> 20 : kTopkBins;
+            const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+            if (bin < kTopkBins && lane == __ffs(peers) - 1)
+                atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+        }
+    }
+    __syncthreads();
+    // Warp 0: the bin of the k-th largest value, scanning from the top (lane l
+    // owns bins 4095 - 128 l down to 3968 - 128 l).
+    if (warp == 0) {
+        constexpr uint32_t kPer = kTopkBins / 32;
+        uint32_t tot = 0;
+        for (uint32_t q = 0; q < kPer; ++q) tot += hist[kTopkBins - 1 - lane * kPer - q];
+        uint32_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += n;
+        }
+        const uint32_t all = __shfl_sync(0xffffffffu, incl, 31);
+        const uint32_t k = cp.top_k;
+        uint32_t found = 0xffffffffu;
+        if (incl - tot < k && k <= incl) {
+            uint32_t run = incl - tot;
+            for (uint32_t q = 0; q < kPer; ++q) {
+                const uint32_t b = kTopkBins - 1 - lane * kPer - q;
+                run += hist[b];
+                if (run >= k) {
+                    found = b;
+                    break;
+                }
+            }
+        }
+        found = __reduce_min_sync(0xffffffffu, found);
+        if (lane == 0) {
+            // Fewer than k candidates: every candidate survives the cut.
+            const float floor_v = all < k ? -3.402823466e38f : key_to_float(found << 20);
+            sm.tau_final[0] = floor_v;
+        }
+    }
+    __syncthreads();
+    // The bin's smallest value as an IEEE bound: a +0 floor also gathers -0.
+    const float floor_v = sm.tau_final[0];
+    CandList &L = sm.list[0];
+    for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
+        float x[kGather];
+#pragma unroll
+        for (uint32_t q = 0; q < kGather; ++q) {
+            const uint32_t i = base + q * kThreads + threadIdx.x;
+            x[q] = i < vocab ? p[i] : kNegInf;
+        }
+#pragma unroll
+        for (uint32_t q = 0; q < kGather; ++q) {
+            const uint32_t i = base + q * kThreads + threadIdx.x;
+            const float v = scale_logit(x[q], scale);
+            const bool take = v != kNegInf && v >= floor_v;
+            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+            if (ballot == 0u) continue;
+            uint32_t at = 0;
+            if (lane == 0) at = atomicAdd(&sm.count[0], static_cast<uint32_t>(__popc(ballot)));
+            at = __shfl_sync(0xffffffffu, at, 0);
+            if (take) {
+                const uint32_t pos = at + __popc(ballot & ((1u << lane) - 1u));
+                if (pos < kCap) {
+                    L.key[pos] = total_key(v);
+                    L.idx[pos] = i;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t count = sm.count[0];
+    if (count > kCap) return false;
+    if (warp == 0)
+        finish_list(sm.fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+    __syncthreads();
+    return true;
+}
+
 // The epilogue's per-row work, kept out of line so that the large-row code's
 // register pressure stays out of the streaming loops.
 __device__ __noinline__ void epilogue_row(const CallParams &cp, const float *p, uint32_t vocab,
@@ -975,7 +1096,10 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     }
                 }
                 const bool last = c + 1 == c1;
-                // Bounds refresh after chunks 2, 4, 8, then every 8, and at the end.
+                // Bounds refresh after chunks 2, 4, 8, then every 8, and at the
+                // end; for k above 64 also after each of the first 4 chunks: the
+                // first chunks' bound is then loose enough to fill the list
+                // before the second chunk ends.
                 const uint32_t done = c + 1 - c0;
                 const bool refresh = last || (done < 8 ? (done & (done - 1)) == 0 && done > 1 : done % 8 == 0);
                 if (!refresh) continue;
@@ -1210,6 +1334,11 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 }
                 continue;
             }
+            if (epilogue_topk_row(cp, logits + row * row_stride, vocab, row, sm,
+                                  reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(&sm.ring[0][0]) +
+                                                               kTopkHistOffset),
+                                  out_ids, out_status, out_probs))
+                continue;
             epilogue_row(cp, logits + row * row_stride, vocab, row,
                          scratch + static_cast<size_t>(slot) * 4u * vocab, out_ids, out_status,
                          out_probs, ls);

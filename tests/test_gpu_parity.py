@@ -399,3 +399,15 @@ def test_vocab_sharded_matches_unsharded(eng, n_shards, top_k):
     assert torch.equal(st, st0)
     assert torch.equal(ids, ids0)
     assert torch.equal(probs.view(torch.int32), probs0.view(torch.int32))
+
+
+@pytest.mark.parametrize("top_k", [100, 128])
+def test_large_k_rows_rescued_exactly(eng, top_k):
+    """k near the streaming limit: the first chunks' bound can admit more
+    candidates than the list holds. Such rows are finished in the CTA's
+    epilogue by a histogram pass and a gather pass (the large-row code only
+    when ties overflow the list too); every row must still match the oracle."""
+    rows, vocab = 48, 151936
+    x = synth.make_logits(rows, vocab, base_seed=4321)
+    u = synth.uniforms(rows, seed=17)
+    compare(eng, x, SamplingParams(0.8, top_k, 0.95), u, f"k{top_k}", check_surv=False)
