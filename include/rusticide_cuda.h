@@ -231,7 +231,8 @@ RSC_API rsc_status rsc_rng_seed(const uint64_t *d_seeds, uint64_t *d_rng_states,
  * fixed-size record per row to d_records (rsc_shard_record_bytes(top_k) bytes
  * each): the shard's scaled row maximum and every logit that can survive
  * the global top-k (at most top_k + RSC_SHARD_TIE_CAP of them, with an
- * overflow count). One streaming pass over the shard; the caller
+ * overflow count). One streaming pass over the shard (rows whose candidates
+ * overflow the pass's list take two more passes in the same launch); the caller
  * all-gathers the records of all ranks (NCCL over NVLink) into a
  * [n_shards][rows] array and calls rsc_shard_merge.
  */

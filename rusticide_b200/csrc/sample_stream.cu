@@ -802,17 +802,25 @@ __device__ __forceinline__ bool streams_row(const CallParams &r, uint32_t vocab)
 // parameters are not the streaming filter's (top-k on, k <= kSmallTopK, a
 // normal scale) or the gather would exceed the list (heavy ties); the row
 // then takes the large-row code.
+// With `rec` (a vocab shard's partial pass) the gathered list becomes the
+// shard's record instead (indices offset by index_offset), cut exactly as a
+// streamed row's record.
 __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const float *p, uint32_t vocab,
                                                size_t row, StreamSmem &sm, uint32_t *hist,
                                                uint32_t *out_ids, int32_t *out_status,
-                                               float *out_probs) {
+                                               float *out_probs, unsigned char *rec,
+                                               uint32_t index_offset) {
     const CallParams cp = for_row(call, row, vocab);
     if (!streams_row(cp, vocab) || !cp.topk_active) return false;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale = cp.scale;
     for (uint32_t b = threadIdx.x; b < kTopkBins; b += kThreads) hist[b] = 0;
-    if (threadIdx.x == 0) sm.count[0] = 0;
+    if (threadIdx.x == 0) {
+        sm.count[0] = 0;
+        sm.csel[0] = 0;  // the row's largest key
+    }
     __syncthreads();
+    uint32_t kmax = 0;
     // Candidates: every scaled value but -inf (NaN reads as -inf). Lanes of a
     // warp that share a bin add once, through their leader. kGather loads per
     // thread are in flight at once.
@@ -828,11 +836,14 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
         for (uint32_t q = 0; q < kGather; ++q) {
             const float v = scale_logit(x[q], scale);
             const uint32_t bin = v != kNegInf ? total_key(v) >> 20 : kTopkBins;
+            if (bin < kTopkBins) kmax = max(kmax, total_key(v));
             const uint32_t peers = __match_any_sync(0xffffffffu, bin);
             if (bin < kTopkBins && lane == __ffs(peers) - 1)
                 atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
         }
     }
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    if (lane == 0 && kmax) atomicMax(&sm.csel[0], kmax);
     __syncthreads();
     // Warp 0: the bin of the k-th largest value, scanning from the top (lane l
     // owns bins 4095 - 128 l down to 3968 - 128 l).
@@ -892,7 +903,7 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
                 const uint32_t pos = at + __popc(ballot & ((1u << lane) - 1u));
                 if (pos < kCap) {
                     L.key[pos] = total_key(v);
-                    L.idx[pos] = i;
+                    L.idx[pos] = i + index_offset;
                 }
             }
         }
@@ -900,8 +911,16 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
     __syncthreads();
     const uint32_t count = sm.count[0];
     if (count > kCap) return false;
-    if (warp == 0)
-        finish_list(sm.fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+    if (warp == 0) {
+        if (rec) {
+            const float M = sm.csel[0] ? key_to_float(sm.csel[0]) : kNegInf;
+            record_list(sm.fw, L.key, L.idx, count, cp, M, 0.0f, 0u, rec,
+                        cp.top_k + RSC_SHARD_TIE_CAP, floor_v);
+        } else {
+            finish_list(sm.fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status,
+                        out_probs);
+        }
+    }
     __syncthreads();
     return true;
 }
@@ -1209,11 +1228,17 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             if (kRecord) {
                 unsigned char *rec = records + row * rec_bytes;
                 if (ov) {
+                    // Rescued in the epilogue while the deferral list has room;
+                    // otherwise the record says so and the merge reports the row.
                     if (lane == 0) {
-                        ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
-                        h->flags = 1;
-                        h->n_cand = 0;
-                        h->n_dropped = 0;
+                        if (sm.ovf_count < kOvfCap) {
+                            sm.ovf_rows[sm.ovf_count++] = static_cast<uint32_t>(row);
+                        } else {
+                            ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                            h->flags = 1;
+                            h->n_cand = 0;
+                            h->n_dropped = 0;
+                        }
                     }
                 } else {
                     float M = kNegInf;
@@ -1304,6 +1329,25 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
     // spin on a lock; holders never wait on anyone) and samples the rows one
     // by one with all its threads.
     __syncthreads();
+    if (kRecord && sm.ovf_count > 0) {
+        // A shard's overflowing rows: the two-pass top-k into their records.
+        uint32_t *hist = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(&sm.ring[0][0]) +
+                                                      kTopkHistOffset);
+        for (uint32_t k = 0; k < sm.ovf_count; ++k) {
+            const size_t row = sm.ovf_rows[k];
+            unsigned char *rec = records + row * rec_bytes;
+            if (!epilogue_topk_row(cp, logits + row * row_stride, vocab, row, sm, hist, nullptr, nullptr,
+                                   nullptr, rec, index_offset)) {
+                if (threadIdx.x == 0) {
+                    ShardRecordHeader *h = reinterpret_cast<ShardRecordHeader *>(rec);
+                    h->flags = 1;
+                    h->n_cand = 0;
+                    h->n_dropped = 0;
+                }
+                __syncthreads();
+            }
+        }
+    }
     if (!kRecord && sm.ovf_count > 0) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         large::LargeSmem<kThreads> &ls = *reinterpret_cast<large::LargeSmem<kThreads> *>(&sm.ring[0][0]);
@@ -1337,7 +1381,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             if (epilogue_topk_row(cp, logits + row * row_stride, vocab, row, sm,
                                   reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(&sm.ring[0][0]) +
                                                                kTopkHistOffset),
-                                  out_ids, out_status, out_probs))
+                                  out_ids, out_status, out_probs, nullptr, 0u))
                 continue;
             epilogue_row(cp, logits + row * row_stride, vocab, row,
                          scratch + static_cast<size_t>(slot) * 4u * vocab, out_ids, out_status,

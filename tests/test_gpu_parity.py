@@ -375,11 +375,14 @@ def test_pick_host_matches_device(eng):
 # ---------------------------------------------------------------------------
 # Vocab-sharded merge, emulated on one GPU (each shard a column slice)
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("n_shards,top_k", [(2, None), (4, None), (8, None), (10, 40), (16, 40)])
+@pytest.mark.parametrize("n_shards,top_k", [(2, None), (4, None), (8, None), (10, 40), (16, 40),
+                                             (8, 100), (4, 128)])
 def test_vocab_sharded_matches_unsharded(eng, n_shards, top_k):
     """Shard records merged into the unsharded result. Up to n_shards * (k + 24)
     = 512 entries per row one warp merges them; beyond (10 and 16 shards at
-    k 40) one block per row does."""
+    k 40, 8 at k 100, 4 at k 128) one block per row does. At k 100 and 128
+    some shard rows overflow the streaming list and are rescued into their
+    records by the partial pass's epilogue."""
     cfg = synth.CONFIGS["cfg4"]
     rows = 16
     x = synth.make_config(cfg, rows=rows, base_seed=606)
