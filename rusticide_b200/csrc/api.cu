@@ -128,7 +128,7 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
     if (rows == 0) return RSC_OK;
     const uint32_t v = static_cast<uint32_t>(vocab);
     const bool small = cp.mode == rsc::kModeSampleLogits && cp.normal_scale &&
-                       ((cp.topk_active && cp.top_k <= rsc::kSmallTopK) ||
+                       ((cp.topk_active && cp.top_k <= rsc::kTwoPassTopK) ||
                         (!cp.topk_active && vocab <= rsc::kSmallCap));
     cudaError_t e;
     if (small) return stream_impl(s, logits, rows, v, row_stride, cp, ids, status, probs, stream);
@@ -151,7 +151,10 @@ rsc_status stream_impl(rsc_sampler *s, const float *logits, size_t rows, uint32_
             const size_t nr = rows - r0 < batch ? rows - r0 : batch;
             if (!s->plan_valid || s->plan_rows != nr || s->plan_vocab != v ||
                 s->plan_topk != (cp.topk_active ? cp.top_k : 0u)) {
-                s->plan = rsc::stream_plan(nr, v, cp.topk_active, cp.top_k, s->num_sms,
+                // Rows with k above the streaming filter's are not streamed:
+                // whole rows, round robin.
+                const bool streamed = cp.topk_active && cp.top_k <= rsc::kSmallTopK;
+                s->plan = rsc::stream_plan(nr, v, streamed, cp.top_k, s->num_sms,
                                            s->max_units * rsc::split_record_bytes(2));
                 s->plan_rows = nr;
                 s->plan_vocab = v;

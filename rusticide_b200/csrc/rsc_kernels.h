@@ -15,6 +15,9 @@ namespace rsc {
 constexpr uint32_t kSmallCap = 512;
 // Largest top_k the streaming kernel takes; larger k go to the large kernel.
 constexpr uint32_t kSmallTopK = kSmallCap / 4;
+// Top-k above kSmallTopK and up to this many: the streaming kernel's two-pass
+// epilogue (a histogram pass and a gather into a kSmallCap list).
+constexpr uint32_t kTwoPassTopK = kSmallCap - 24;
 
 cudaError_t launch_greedy(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                           uint32_t *out_ids, int32_t *out_status, int num_sms,

@@ -97,8 +97,11 @@ struct StreamSmem {
 static_assert(sizeof(large::LargeSmem<kThreads>) <= sizeof(float) * kStages * kChunk,
               "the epilogue's large-row workspace lives in the idle ring");
 // The epilogue's top-k histogram (4096 bins) sits in the idle ring after the
-// large-row workspace.
+// large-row workspace. Its gather serves k up to kTwoPassMaxK (the list keeps
+// room for ties).
 constexpr uint32_t kTopkBins = 4096;
+constexpr uint32_t kTwoPassMaxK = kCap - RSC_SHARD_TIE_CAP;
+static_assert(kTwoPassMaxK == kTwoPassTopK, "the host routes exactly the k the epilogue serves");
 constexpr size_t kTopkHistOffset = (sizeof(large::LargeSmem<kThreads>) + 255) & ~static_cast<size_t>(255);
 static_assert(kTopkHistOffset + kTopkBins * sizeof(uint32_t) <= sizeof(float) * kStages * kChunk,
               "the top-k histogram fits the idle ring beside the large-row workspace");
@@ -811,20 +814,17 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
                                                float *out_probs, unsigned char *rec,
                                                uint32_t index_offset) {
     const CallParams cp = for_row(call, row, vocab);
-    if (!streams_row(cp, vocab) || !cp.topk_active) return false;
+    if (cp.mode != kModeSampleLogits || !cp.normal_scale || !cp.topk_active || cp.top_k > kTwoPassMaxK)
+        return false;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale = cp.scale;
-    for (uint32_t b = threadIdx.x; b < kTopkBins; b += kThreads) hist[b] = 0;
-    if (threadIdx.x == 0) {
-        sm.count[0] = 0;
-        sm.csel[0] = 0;  // the row's largest key
-    }
-    __syncthreads();
-    uint32_t kmax = 0;
-    // Candidates: every scaled value but -inf (NaN reads as -inf). Lanes of a
-    // warp that share a bin add once, through their leader. kGather loads per
-    // thread are in flight at once.
-    constexpr uint32_t kGather = 16;
+    constexpr uint32_t kGather = 16;  // loads per thread in flight at once
+    // Pass 0: each thread's two largest candidates (every scaled value but
+    // -inf; NaN reads as -inf). The k-th largest of these 2 x kThreads values
+    // has k distinct values at or above it, so it bounds the row's k-th value
+    // from below: the histogram then counts only the values at or above it,
+    // and its few hot bins see few atomics.
+    float m1 = kNegInf, m2 = kNegInf;
     for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
         float x[kGather];
 #pragma unroll
@@ -835,18 +835,56 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
 #pragma unroll
         for (uint32_t q = 0; q < kGather; ++q) {
             const float v = scale_logit(x[q], scale);
-            const uint32_t bin = v != kNegInf ? total_key(v) >> 20 : kTopkBins;
-            if (bin < kTopkBins) kmax = max(kmax, total_key(v));
+            if (v > m1) {
+                m2 = m1;
+                m1 = v;
+            } else if (v > m2) {
+                m2 = v;
+            }
+        }
+    }
+    // Key 0 (a NaN pattern) stands for "no candidate".
+    hist[threadIdx.x] = m1 != kNegInf ? total_key(m1) : 0u;
+    hist[kThreads + threadIdx.x] = m2 != kNegInf ? total_key(m2) : 0u;
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, hist[threadIdx.x]);
+    if (threadIdx.x == 0) {
+        sm.count[0] = 0;
+        sm.csel[0] = 0;  // the row's largest key
+    }
+    __syncthreads();
+    if (lane == 0 && kmax) atomicMax(&sm.csel[0], kmax);
+    float bound = -3.402823466e38f;
+    if (cp.top_k <= 2u * kThreads) {
+        const uint32_t bkey = group_select_kth_largest<kThreads, SyncBlock>(
+            2u * kThreads, cp.top_k, [&](uint32_t i) { return hist[i]; }, hist + 1024, hist + 1280);
+        if (bkey) bound = key_to_float(bkey);
+    }
+    __syncthreads();
+    for (uint32_t b = threadIdx.x; b < kTopkBins; b += kThreads) hist[b] = 0;
+    __syncthreads();
+    // Pass 1: the histogram of the top 12 key bits of the values at or above
+    // the bound. Lanes of a warp that share a bin add once, through their
+    // leader.
+    for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
+        float x[kGather];
+#pragma unroll
+        for (uint32_t q = 0; q < kGather; ++q) {
+            const uint32_t i = base + q * kThreads + threadIdx.x;
+            x[q] = i < vocab ? p[i] : kNegInf;
+        }
+#pragma unroll
+        for (uint32_t q = 0; q < kGather; ++q) {
+            const float v = scale_logit(x[q], scale);
+            const uint32_t bin = (v != kNegInf && v >= bound) ? total_key(v) >> 20 : kTopkBins;
             const uint32_t peers = __match_any_sync(0xffffffffu, bin);
             if (bin < kTopkBins && lane == __ffs(peers) - 1)
                 atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
         }
     }
-    kmax = __reduce_max_sync(0xffffffffu, kmax);
-    if (lane == 0 && kmax) atomicMax(&sm.csel[0], kmax);
     __syncthreads();
     // Warp 0: the bin of the k-th largest value, scanning from the top (lane l
-    // owns bins 4095 - 128 l down to 3968 - 128 l).
+    // owns bins 4095 - 128 l down to 3968 - 128 l). chist[0..2] get the bin,
+    // the candidates above it and the bin's own population.
     if (warp == 0) {
         constexpr uint32_t kPer = kTopkBins / 32;
         uint32_t tot = 0;
@@ -859,24 +897,84 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
         }
         const uint32_t all = __shfl_sync(0xffffffffu, incl, 31);
         const uint32_t k = cp.top_k;
-        uint32_t found = 0xffffffffu;
         if (incl - tot < k && k <= incl) {
             uint32_t run = incl - tot;
             for (uint32_t q = 0; q < kPer; ++q) {
                 const uint32_t b = kTopkBins - 1 - lane * kPer - q;
-                run += hist[b];
-                if (run >= k) {
-                    found = b;
+                if (run + hist[b] >= k) {
+                    sm.chist[0] = b;
+                    sm.chist[1] = run;
+                    sm.chist[2] = hist[b];
                     break;
                 }
+                run += hist[b];
             }
         }
-        found = __reduce_min_sync(0xffffffffu, found);
-        if (lane == 0) {
+        if (lane == 0 && all < k) {
             // Fewer than k candidates: every candidate survives the cut.
-            const float floor_v = all < k ? -3.402823466e38f : key_to_float(found << 20);
-            sm.tau_final[0] = floor_v;
+            sm.chist[0] = 0xffffffffu;
+            sm.tau_final[0] = -3.402823466e38f;
         }
+    }
+    __syncthreads();
+    const uint32_t kbin = sm.chist[0];
+    if (kbin != 0xffffffffu) {
+        uint32_t floor_key = kbin << 20;
+        if (sm.chist[1] + sm.chist[2] > kCap) {
+            // The k-th value's bin holds more candidates than the list: one
+            // more histogram, of the next 12 key bits inside that bin.
+            const uint32_t above = sm.chist[1];
+            __syncthreads();
+            for (uint32_t b = threadIdx.x; b < kTopkBins; b += kThreads) hist[b] = 0;
+            __syncthreads();
+            for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
+                float x[kGather];
+#pragma unroll
+                for (uint32_t q = 0; q < kGather; ++q) {
+                    const uint32_t i = base + q * kThreads + threadIdx.x;
+                    x[q] = i < vocab ? p[i] : kNegInf;
+                }
+#pragma unroll
+                for (uint32_t q = 0; q < kGather; ++q) {
+                    const float v = scale_logit(x[q], scale);
+                    const uint32_t key = total_key(v);
+                    const uint32_t sub = (v != kNegInf && v >= bound && (key >> 20) == kbin)
+                                             ? (key >> 8) & 0xfffu
+                                             : kTopkBins;
+                    const uint32_t peers = __match_any_sync(0xffffffffu, sub);
+                    if (sub < kTopkBins && lane == __ffs(peers) - 1)
+                        atomicAdd(&hist[sub], static_cast<uint32_t>(__popc(peers)));
+                }
+            }
+            __syncthreads();
+            if (warp == 0) {
+                constexpr uint32_t kPer = kTopkBins / 32;
+                uint32_t tot = 0;
+                for (uint32_t q = 0; q < kPer; ++q) tot += hist[kTopkBins - 1 - lane * kPer - q];
+                uint32_t incl = tot;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += n;
+                }
+                const uint32_t k = cp.top_k - above;  // still to find inside the bin
+                if (incl - tot < k && k <= incl) {
+                    uint32_t run = incl - tot;
+                    for (uint32_t q = 0; q < kPer; ++q) {
+                        const uint32_t b = kTopkBins - 1 - lane * kPer - q;
+                        if (run + hist[b] >= k) {
+                            sm.chist[3] = b;
+                            break;
+                        }
+                        run += hist[b];
+                    }
+                }
+            }
+            __syncthreads();
+            floor_key |= sm.chist[3] << 8;
+        }
+        // Both the bin floor and the pass-0 bound are at most the k-th value.
+        if (threadIdx.x == 0) sm.tau_final[0] = fmaxf(key_to_float(floor_key), bound);
     }
     __syncthreads();
     // The bin's smallest value as an IEEE bound: a +0 floor also gathers -0.
@@ -1010,7 +1108,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             uint32_t *ovf = &sm.overflow[b];
             const RowGeom g = row_geom(logits, row, row_stride, vocab);
             const uint32_t c0 = pc.c0;
-            const uint32_t c1 = min(pc.c1, g.nchunks);
+            const uint32_t c1 = live ? min(pc.c1, g.nchunks) : c0;  // the producer skips it
             // Candidates satisfy v >= tau. -FLT_MAX admits everything but -inf and
             // NaN (NaN reads as -inf in the reference, and -inf never survives);
             // an IEEE compare also admits -0.0 against +0.0, as the keep test does.
@@ -1182,6 +1280,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         bool ok = true;
         Piece pc;
         for (uint32_t u = 0; ok && get_piece(rows, nch, streamk, u, pc); ++u) {
+            // A row the filter cannot serve is not streamed: its consumers
+            // hand over an overflowed list and the epilogue samples it.
+            if (kRows && !streams_row(for_row(cp, pc.row, vocab), vocab)) continue;
             const RowGeom g = row_geom(logits, pc.row, row_stride, vocab);
             const uint32_t c1 = min(pc.c1, g.nchunks);
             for (uint32_t c = pc.c0; c < c1; ++c) {
@@ -1352,25 +1453,37 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
         asm volatile("griddepcontrol.wait;" ::: "memory");
         large::LargeSmem<kThreads> &ls = *reinterpret_cast<large::LargeSmem<kThreads> *>(&sm.ring[0][0]);
         load_exp_table(ls.exp_tab);
-        if (threadIdx.x == 0) {
-            uint32_t got = ~0u;
-            const unsigned long long t0 = global_ns();
-            for (uint32_t i = 0; got == ~0u; ++i) {
-                const uint32_t s = (blockIdx.x + i) % slots;
-                if (atomicCAS(&slot_lock[s], 0u, 1u) == 0u) {
-                    got = s;
-                    break;
-                }
-                if (global_ns() - t0 > kWaitLimitNs) break;
-                __nanosleep(1000);
-            }
-            __threadfence();
-            sm.slot = got;
-        }
-        __syncthreads();
-        const uint32_t slot = sm.slot;
+        uint32_t *hist = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(&sm.ring[0][0]) +
+                                                      kTopkHistOffset);
+        // A scratch slot is taken only for a row that needs the large-row code
+        // (a bounded spin on a lock; holders never wait on anyone).
+        uint32_t slot = ~0u;
+        bool tried = false;
         for (uint32_t k = 0; k < sm.ovf_count; ++k) {
             const size_t row = sm.ovf_rows[k];
+            if (epilogue_topk_row(cp, logits + row * row_stride, vocab, row, sm, hist, out_ids,
+                                  out_status, out_probs, nullptr, 0u))
+                continue;
+            if (!tried) {
+                tried = true;
+                if (threadIdx.x == 0) {
+                    uint32_t got = ~0u;
+                    const unsigned long long t0 = global_ns();
+                    for (uint32_t i = 0; got == ~0u; ++i) {
+                        const uint32_t s = (blockIdx.x + i) % slots;
+                        if (atomicCAS(&slot_lock[s], 0u, 1u) == 0u) {
+                            got = s;
+                            break;
+                        }
+                        if (global_ns() - t0 > kWaitLimitNs) break;
+                        __nanosleep(1000);
+                    }
+                    __threadfence();
+                    sm.slot = got;
+                }
+                __syncthreads();
+                slot = sm.slot;
+            }
             if (slot == ~0u) {
                 if (threadIdx.x == 0) {
                     out_ids[row] = 0;
@@ -1378,11 +1491,6 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 }
                 continue;
             }
-            if (epilogue_topk_row(cp, logits + row * row_stride, vocab, row, sm,
-                                  reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(&sm.ring[0][0]) +
-                                                               kTopkHistOffset),
-                                  out_ids, out_status, out_probs, nullptr, 0u))
-                continue;
             epilogue_row(cp, logits + row * row_stride, vocab, row,
                          scratch + static_cast<size_t>(slot) * 4u * vocab, out_ids, out_status,
                          out_probs, ls);
@@ -1711,7 +1819,10 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
                                void *seg_records, uint32_t *row_arrivals, uint32_t *scratch,
                                uint32_t slots, uint32_t *slot_lock, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
-    auto kernel = p.row_params ? stream_topk_kernel<false, true> : stream_topk_kernel<false, false>;
+    // The per-row instance also serves calls whose k is above the streaming
+    // filter's: every row goes straight to the epilogue's two passes.
+    const bool rows_instance = p.row_params || (p.topk_active && p.top_k > kSmallTopK);
+    auto kernel = rows_instance ? stream_topk_kernel<false, true> : stream_topk_kernel<false, false>;
     cudaError_t e = prepare(kernel, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};

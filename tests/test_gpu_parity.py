@@ -414,3 +414,15 @@ def test_large_k_rows_rescued_exactly(eng, top_k):
     x = synth.make_logits(rows, vocab, base_seed=4321)
     u = synth.uniforms(rows, seed=17)
     compare(eng, x, SamplingParams(0.8, top_k, 0.95), u, f"k{top_k}", check_surv=False)
+
+
+@pytest.mark.parametrize("top_k,vocab,check_surv", [(200, 151936, False), (488, 151936, False),
+                                                    (300, 32000, True)])
+def test_topk_above_streaming_limit(eng, top_k, vocab, check_surv):
+    """128 < k <= 488: rows are not streamed but finished by the two-pass
+    top-k (histogram, gather, exact finisher) in the streaming kernel's
+    epilogue; ids, probabilities and survivor sets must match the oracle."""
+    rows = 24
+    x = synth.make_logits(rows, vocab, base_seed=top_k)
+    u = synth.uniforms(rows, seed=top_k + 1)
+    compare(eng, x, SamplingParams(0.8, top_k, 0.95), u, f"k{top_k}", check_surv=check_surv)
