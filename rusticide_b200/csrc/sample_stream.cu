@@ -818,31 +818,55 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
         return false;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float scale = cp.scale;
-    constexpr uint32_t kGather = 16;  // loads per thread in flight at once
+    // Every pass visits the row's scaled values with one call of fn(v, i)
+    // per value and the same number of calls in every thread (fn may use
+    // warp-collective operations; values past the row come as -inf): a scalar
+    // head up to 16-byte alignment and a scalar tail (a single call each),
+    // and the body in float4 loads, kGather4 of them in flight per thread.
+    constexpr uint32_t kGather4 = 8;
+    const uint32_t mis = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(p) >> 2) & 3u);
+    const uint32_t head = mis ? min(vocab, 4u - mis) : 0u;
+    const uint32_t n4 = (vocab - head) / 4u;
+    const uint32_t tail0 = head + 4u * n4;
+    const float4 *p4 = reinterpret_cast<const float4 *>(p + head);
+    auto visit = [&](auto &&fn) {
+        {
+            uint32_t i = ~0u;
+            if (threadIdx.x < head) i = threadIdx.x;
+            else if (threadIdx.x >= 32 && threadIdx.x - 32 < vocab - tail0) i = tail0 + threadIdx.x - 32;
+            fn(i != ~0u ? scale_logit(p[i], scale) : kNegInf, i);
+        }
+        for (uint32_t base = 0; base < n4; base += kThreads * kGather4) {
+            float4 f[kGather4];
+#pragma unroll
+            for (uint32_t q = 0; q < kGather4; ++q) {
+                const uint32_t j = base + q * kThreads + threadIdx.x;
+                f[q] = j < n4 ? p4[j] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+            }
+#pragma unroll
+            for (uint32_t q = 0; q < kGather4; ++q) {
+                const uint32_t i = head + 4u * (base + q * kThreads + threadIdx.x);
+                fn(scale_logit(f[q].x, scale), i);
+                fn(scale_logit(f[q].y, scale), i + 1u);
+                fn(scale_logit(f[q].z, scale), i + 2u);
+                fn(scale_logit(f[q].w, scale), i + 3u);
+            }
+        }
+    };
     // Pass 0: each thread's two largest candidates (every scaled value but
     // -inf; NaN reads as -inf). The k-th largest of these 2 x kThreads values
     // has k distinct values at or above it, so it bounds the row's k-th value
     // from below: the histogram then counts only the values at or above it,
     // and its few hot bins see few atomics.
     float m1 = kNegInf, m2 = kNegInf;
-    for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
-        float x[kGather];
-#pragma unroll
-        for (uint32_t q = 0; q < kGather; ++q) {
-            const uint32_t i = base + q * kThreads + threadIdx.x;
-            x[q] = i < vocab ? p[i] : kNegInf;
+    visit([&](float v, uint32_t) {
+        if (v > m1) {
+            m2 = m1;
+            m1 = v;
+        } else if (v > m2) {
+            m2 = v;
         }
-#pragma unroll
-        for (uint32_t q = 0; q < kGather; ++q) {
-            const float v = scale_logit(x[q], scale);
-            if (v > m1) {
-                m2 = m1;
-                m1 = v;
-            } else if (v > m2) {
-                m2 = v;
-            }
-        }
-    }
+    });
     // Key 0 (a NaN pattern) stands for "no candidate".
     hist[threadIdx.x] = m1 != kNegInf ? total_key(m1) : 0u;
     hist[kThreads + threadIdx.x] = m2 != kNegInf ? total_key(m2) : 0u;
@@ -865,22 +889,14 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
     // Pass 1: the histogram of the top 12 key bits of the values at or above
     // the bound. Lanes of a warp that share a bin add once, through their
     // leader.
-    for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
-        float x[kGather];
-#pragma unroll
-        for (uint32_t q = 0; q < kGather; ++q) {
-            const uint32_t i = base + q * kThreads + threadIdx.x;
-            x[q] = i < vocab ? p[i] : kNegInf;
-        }
-#pragma unroll
-        for (uint32_t q = 0; q < kGather; ++q) {
-            const float v = scale_logit(x[q], scale);
-            const uint32_t bin = (v != kNegInf && v >= bound) ? total_key(v) >> 20 : kTopkBins;
-            const uint32_t peers = __match_any_sync(0xffffffffu, bin);
-            if (bin < kTopkBins && lane == __ffs(peers) - 1)
-                atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
-        }
-    }
+    visit([&](float v, uint32_t) {
+        const bool counted = v != kNegInf && v >= bound;
+        if (!__any_sync(0xffffffffu, counted)) return;  // most warps, with a tight bound
+        const uint32_t bin = counted ? total_key(v) >> 20 : kTopkBins;
+        const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+        if (counted && lane == __ffs(peers) - 1)
+            atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+    });
     __syncthreads();
     // Warp 0: the bin of the k-th largest value, scanning from the top (lane l
     // owns bins 4095 - 128 l down to 3968 - 128 l). chist[0..2] get the bin,
@@ -927,25 +943,15 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
             __syncthreads();
             for (uint32_t b = threadIdx.x; b < kTopkBins; b += kThreads) hist[b] = 0;
             __syncthreads();
-            for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
-                float x[kGather];
-#pragma unroll
-                for (uint32_t q = 0; q < kGather; ++q) {
-                    const uint32_t i = base + q * kThreads + threadIdx.x;
-                    x[q] = i < vocab ? p[i] : kNegInf;
-                }
-#pragma unroll
-                for (uint32_t q = 0; q < kGather; ++q) {
-                    const float v = scale_logit(x[q], scale);
-                    const uint32_t key = total_key(v);
-                    const uint32_t sub = (v != kNegInf && v >= bound && (key >> 20) == kbin)
-                                             ? (key >> 8) & 0xfffu
-                                             : kTopkBins;
-                    const uint32_t peers = __match_any_sync(0xffffffffu, sub);
-                    if (sub < kTopkBins && lane == __ffs(peers) - 1)
-                        atomicAdd(&hist[sub], static_cast<uint32_t>(__popc(peers)));
-                }
-            }
+            visit([&](float v, uint32_t) {
+                const uint32_t key = total_key(v);
+                const bool counted = v != kNegInf && v >= bound && (key >> 20) == kbin;
+                if (!__any_sync(0xffffffffu, counted)) return;
+                const uint32_t sub = counted ? (key >> 8) & 0xfffu : kTopkBins;
+                const uint32_t peers = __match_any_sync(0xffffffffu, sub);
+                if (counted && lane == __ffs(peers) - 1)
+                    atomicAdd(&hist[sub], static_cast<uint32_t>(__popc(peers)));
+            });
             __syncthreads();
             if (warp == 0) {
                 constexpr uint32_t kPer = kTopkBins / 32;
@@ -980,32 +986,21 @@ __device__ __noinline__ bool epilogue_topk_row(const CallParams &call, const flo
     // The bin's smallest value as an IEEE bound: a +0 floor also gathers -0.
     const float floor_v = sm.tau_final[0];
     CandList &L = sm.list[0];
-    for (uint32_t base = 0; base < vocab; base += kThreads * kGather) {
-        float x[kGather];
-#pragma unroll
-        for (uint32_t q = 0; q < kGather; ++q) {
-            const uint32_t i = base + q * kThreads + threadIdx.x;
-            x[q] = i < vocab ? p[i] : kNegInf;
-        }
-#pragma unroll
-        for (uint32_t q = 0; q < kGather; ++q) {
-            const uint32_t i = base + q * kThreads + threadIdx.x;
-            const float v = scale_logit(x[q], scale);
-            const bool take = v != kNegInf && v >= floor_v;
-            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-            if (ballot == 0u) continue;
-            uint32_t at = 0;
-            if (lane == 0) at = atomicAdd(&sm.count[0], static_cast<uint32_t>(__popc(ballot)));
-            at = __shfl_sync(0xffffffffu, at, 0);
-            if (take) {
-                const uint32_t pos = at + __popc(ballot & ((1u << lane) - 1u));
-                if (pos < kCap) {
-                    L.key[pos] = total_key(v);
-                    L.idx[pos] = i + index_offset;
-                }
+    visit([&](float v, uint32_t i) {
+        const bool take = v != kNegInf && v >= floor_v;
+        const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+        if (ballot == 0u) return;
+        uint32_t at = 0;
+        if (lane == 0) at = atomicAdd(&sm.count[0], static_cast<uint32_t>(__popc(ballot)));
+        at = __shfl_sync(0xffffffffu, at, 0);
+        if (take) {
+            const uint32_t pos = at + __popc(ballot & ((1u << lane) - 1u));
+            if (pos < kCap) {
+                L.key[pos] = total_key(v);
+                L.idx[pos] = i + index_offset;
             }
         }
-    }
+    });
     __syncthreads();
     const uint32_t count = sm.count[0];
     if (count > kCap) return false;
