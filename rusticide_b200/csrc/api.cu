@@ -221,8 +221,8 @@ rsc_status rsc_sampler_create(int device, size_t max_rows, size_t max_vocab, rsc
     s->max_rows = max_rows < 1 ? 1 : max_rows;
     s->max_vocab = max_vocab < 1 ? 1 : max_vocab;
     cudaError_t e = cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, device);
-    // One large-survivor CTA per SM, at most one per row.
-    size_t slots = static_cast<size_t>(s->num_sms);
+    // kLargeCtasPerSm large-survivor CTAs per SM, at most one per row.
+    size_t slots = static_cast<size_t>(s->num_sms) * rsc::kLargeCtasPerSm;
     if (slots > s->max_rows) slots = s->max_rows;
     s->large_slots = static_cast<uint32_t>(slots);
     if (e == cudaSuccess) e = cudaMalloc(&s->slot_lock, s->large_slots * sizeof(uint32_t));

@@ -100,10 +100,11 @@ extern "C" RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t r
     cp.out_surv = nullptr;
     cp.surv_cap = 0;
 
-    // Rows sampled at once: one per SM, as many as the scratch holds.
+    // Rows sampled at once: kLargeCtasPerSm per SM, as many as the scratch holds.
     const size_t per_row = 4 * (vocab > 0 ? vocab : 1);
     size_t slots = kScratchWords / per_row;
-    if (slots > static_cast<size_t>(s->num_sms)) slots = static_cast<size_t>(s->num_sms);
+    const size_t resident = static_cast<size_t>(s->num_sms) * rsc::kLargeCtasPerSm;
+    if (slots > resident) slots = resident;
     if (slots > rows) slots = rows;
     cudaError_t e = rsc::launch_large(d_logits, rows, static_cast<uint32_t>(vocab), row_stride, cp,
                                       d_out_ids, d_out_status, d_out_probs,

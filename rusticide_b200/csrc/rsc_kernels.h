@@ -69,6 +69,12 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
 
 // Large-survivor kernel over rows [0, rows), one 512-thread block per row.
 // Scratch: `slots` regions of 4 * vocab uint32 each.
+// Large-survivor kernel: resident CTAs per SM. Each CTA samples one row at a
+// time, with its own scratch slot of 4 * vocab words. Its per-row code is a
+// chain of block scans and barriers; two CTAs per SM overlap one's barriers
+// with the other's work (cap: 64 registers a thread at 512 threads).
+constexpr uint32_t kLargeCtasPerSm = 2;
+
 cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, uint32_t *scratch, uint32_t slots, cudaStream_t stream);

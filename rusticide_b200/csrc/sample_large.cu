@@ -11,7 +11,7 @@ using namespace large;
 
 constexpr int kThreads = 512;
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, kLargeCtasPerSm)
 large_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab, size_t row_stride,
              CallParams cp, uint32_t *__restrict__ out_ids, int32_t *__restrict__ out_status,
              float *__restrict__ out_probs, uint32_t *__restrict__ scratch) {
