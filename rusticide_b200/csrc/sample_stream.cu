@@ -744,7 +744,11 @@ __device__ __forceinline__ uint32_t chunk_owner(unsigned long long x, unsigned l
     return static_cast<uint32_t>(((x + 1ull) * G - 1ull) / T);
 }
 
-// The u-th piece of this CTA; false past the last.
+// The u-th piece of this CTA; false past the last. Under the balanced
+// schedule a CTA takes its last piece (in row order) first: that piece is
+// the head of a row whose tail the next CTA also streams first, so both parts
+// of every split row arrive early and the row's merge overlaps streaming. The
+// CTA then ends on one of its whole rows, which needs no merge.
 __device__ __forceinline__ bool get_piece(size_t rows, uint32_t nch, uint32_t streamk, uint32_t u,
                                           Piece &pc) {
     if (!streamk) {
@@ -761,9 +765,15 @@ __device__ __forceinline__ bool get_piece(size_t rows, uint32_t nch, uint32_t st
     const unsigned long long G = gridDim.x;
     const unsigned long long begin = T * blockIdx.x / G;
     const unsigned long long end = T * (blockIdx.x + 1ull) / G;
-    const size_t row = static_cast<size_t>(begin / nch) + u;
+    // Pieces: the rows r >= begin / nch that start before `end` (an empty
+    // range inside a row still makes one empty piece of it).
+    const size_t first_row = static_cast<size_t>(begin / nch);
+    const unsigned long long frs = static_cast<unsigned long long>(first_row) * nch;
+    const uint32_t npieces =
+        frs < end ? static_cast<uint32_t>((end + nch - 1ull) / nch - first_row) : 0u;
+    if (u >= npieces) return false;
+    const size_t row = first_row + (u == 0 ? npieces - 1u : u - 1u);
     const unsigned long long rs = static_cast<unsigned long long>(row) * nch;
-    if (rs >= end) return false;
     pc.row = row;
     pc.c0 = static_cast<uint32_t>((begin > rs ? begin : rs) - rs);
     pc.c1 = static_cast<uint32_t>((end < rs + nch ? end : rs + nch) - rs);
