@@ -62,6 +62,8 @@ struct CandList {
 // Lists up to this size are ordered by ranks (each lane counts, for its few
 // entries, the entries that precede them) instead of radix select and sorts.
 constexpr uint32_t kRankMax = 128;
+// No list to finish (a finisher piece that only publishes or defers).
+constexpr uint32_t kNoList = 0xffffffffu;
 
 // Workspace of one finishing warp.
 struct FinishWork {
@@ -1331,6 +1333,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             uint32_t cnt = sm.count[b];
             const bool ov = sm.overflow[b] != 0 || cnt > kCap;
             if (!ov && rp.topk_active) cnt = precut_list(sm.list[b], cnt, sm.tau_final[b]);
+            uint32_t fin_count = kNoList;  // the list to finish, if any
             if (kRecord) {
                 unsigned char *rec = records + row * rec_bytes;
                 if (ov) {
@@ -1356,8 +1359,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 if (ov) {
                     if (lane == 0) defer_row(sm, row, out_ids, out_status);
                 } else {
-                    finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, cnt, rp, row,
-                                out_ids, out_status, out_probs);
+                    fin_count = cnt;
                 }
             } else {
                 // One part of a split row: publish its record, and the part
@@ -1389,12 +1391,18 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     if (!ok) {
                         if (lane == 0) defer_row(sm, row, out_ids, out_status);
                     } else {
-                        finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, n, rp, row,
-                                    out_ids, out_status, out_probs);
+                        fin_count = n;
                     }
-                    if (lane == 0) row_arrivals[row] = 0;  // ready for the next call
+                    // Ready for the next call, whose finisher writes only after
+                    // this grid completes (griddepcontrol.wait).
+                    if (lane == 0) row_arrivals[row] = 0;
                 }
             }
+            // One call site for whole rows and merged split rows: the final
+            // whole row then runs code the CTA's earlier merges have fetched.
+            if (fin_count != kNoList)
+                finish_list(sm.fw, sm.exp_tab, sm.list[b].key, sm.list[b].idx, fin_count, rp, row,
+                            out_ids, out_status, out_probs);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.list_empty[b]);
         }
