@@ -223,6 +223,18 @@ def test_configs_match_oracle(eng, name, rows):
     compare(eng, x, params, u, name, check_surv=True)
 
 
+@pytest.mark.parametrize("rows,vocab,top_k", [(1, 1_000_000, 40), (4, 400_000, 40), (2, 262_144, 100),
+                                             (3, 800_000, 8), (1, 1_000_000, 8)])
+def test_split_rows_many_parts(eng, rows, vocab, top_k):
+    """Small batches of long rows: the balanced schedule spreads each row over
+    several CTAs (parts of at least 16 chunks; 8, 6, 4, 12 and 15 parts for
+    these shapes on 148 SMs), and the last part to arrive merges the parts'
+    records before the row is finished."""
+    x = synth.make_logits(rows, vocab, base_seed=vocab + rows)
+    u = synth.uniforms(rows, seed=rows)
+    compare(eng, x, SamplingParams(0.8, top_k, 0.95), u, f"{rows}x{vocab} k={top_k}")
+
+
 @pytest.mark.parametrize("name,rows", [("cfg0_greedy", 1), ("cfg1_greedy", 16)])
 def test_greedy_configs(eng, name, rows):
     cfg = synth.CONFIGS[name]
