@@ -82,7 +82,11 @@ RSC_API int rsc_abi_version(void);
 /*
  * Creates a sampler on `device` for batches of up to max_rows rows of up to
  * max_vocab logits. Allocates its scratch memory here, once; the sampling
- * calls allocate nothing. Replaces `Sampler::new(seed)`
+ * calls allocate nothing. The largest parts, in bytes:
+ *   - whole-row sort scratch: min(2 x SMs, max_rows) x max_vocab x 16
+ *     (about 720 MB at 296 rows of 151936 on a 148-SM B200);
+ *   - staging for rsc_pick_host: max_rows x max_vocab x 4.
+ * Replaces `Sampler::new(seed)`
  * (crates/rusticide-sampling/src/sampler.rs:17-23) for a batch: per-row
  * generator states are the caller's d_rng_states array (rsc_rng_seed).
  */
