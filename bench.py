@@ -36,6 +36,27 @@ sys.path.insert(0, str(ROOT))
 
 L2_BYTES = 126 * 1024 * 1024
 
+# The JSON line is the only output on stdout. Everything else written to file
+# descriptor 1, by Python or by native libraries (NCCL prints its version there
+# on some systems), goes to stderr; emit() writes to the original stdout.
+_JSON_FD = None
+
+
+def claim_stdout() -> None:
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
 
 def env_int(name: str, default: int) -> int:
     try:
@@ -242,10 +263,11 @@ def run_reference(args, cfg, rank: int, world: int) -> None:
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference = C++ restatement of rusticide-sampling (Rust toolchain absent on this image)",
     }
-    print(json.dumps(line))
+    emit(line)
 
 
 def main() -> None:
+    claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10000)
@@ -466,7 +488,7 @@ def main() -> None:
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
-    print(json.dumps(line))
+    emit(line)
 
 
 if __name__ == "__main__":

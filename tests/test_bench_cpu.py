@@ -1,0 +1,30 @@
+"""bench.py's output contract, checked on the CPU through its reference arm:
+exactly one JSON line on stdout with the metric, the timing fields and the
+reference arm's cpu_baseline and e2e objects. Everything else the run prints
+(argparse, native libraries such as NCCL) belongs on stderr."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_reference_arm_prints_one_json_line(oracle_lib):
+    r = subprocess.run(
+        [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", "cfg0",
+         "--steps", "3", "--warmup", "3", "--ref-seconds", "5"],
+        capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.splitlines()
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "dtype", "config", "impl", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference"
+    assert d["value"] > 0 and d["steps"] == 3 and d["warmup"] == 3
+    assert d["config"]["workload"] == "cfg0"
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["kind"] in ("port", "reference")
