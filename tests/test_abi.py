@@ -62,3 +62,15 @@ def test_header_compiles_as_c():
     res = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(ROOT / "include"), "-x", "c",
                           "-", "-o", "/dev/null"], input=src, capture_output=True, text=True)
     assert res.returncode == 0, res.stderr
+
+
+def test_rust_binding_declares_every_symbol():
+    """rust/rusticide-cuda/src/ffi.rs is the binding a Rust caller links (it is
+    not compiled here: no Rust toolchain on this image), so its extern block is
+    checked as text against the header."""
+    ffi = (ROOT / "rust" / "rusticide-cuda" / "src" / "ffi.rs").read_text()
+    bound = set(re.findall(r"\bfn\s+(rsc_\w+)\s*\(", ffi))
+    missing = declared_symbols() - bound
+    assert not missing, f"declared in the header but not bound in ffi.rs: {sorted(missing)}"
+    extra = bound - declared_symbols()
+    assert not extra, f"bound in ffi.rs but not declared in the header: {sorted(extra)}"
