@@ -74,3 +74,19 @@ def test_rust_binding_declares_every_symbol():
     assert not missing, f"declared in the header but not bound in ffi.rs: {sorted(missing)}"
     extra = bound - declared_symbols()
     assert not extra, f"bound in ffi.rs but not declared in the header: {sorted(extra)}"
+
+
+def test_rust_binding_parameter_counts_match_the_header():
+    header = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "rusticide_cuda.h").read_text(), flags=re.S)
+    want = {}
+    for m in re.finditer(r"RSC_API\s+[^;(]*?\b(rsc_\w+)\s*\(([^;]*?)\)\s*;", header, flags=re.S):
+        args = m.group(2).strip()
+        want[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    ffi = (ROOT / "rust" / "rusticide-cuda" / "src" / "ffi.rs").read_text()
+    got = {}
+    for m in re.finditer(r"\bfn\s+(rsc_\w+)\s*\(([^)]*)\)", ffi, flags=re.S):
+        args = m.group(2).strip().rstrip(",")
+        got[m.group(1)] = 0 if not args else args.count(",") + 1
+    assert want, "no declarations parsed from the header"
+    mismatched = {k: (want[k], got.get(k)) for k in want if want[k] != got.get(k)}
+    assert not mismatched, f"(header, ffi.rs) parameter counts differ: {mismatched}"
