@@ -76,12 +76,25 @@ def test_rust_binding_declares_every_symbol():
     assert not extra, f"bound in ffi.rs but not declared in the header: {sorted(extra)}"
 
 
-def test_rust_binding_parameter_counts_match_the_header():
+def header_parameter_counts() -> dict[str, int]:
     header = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "rusticide_cuda.h").read_text(), flags=re.S)
     want = {}
     for m in re.finditer(r"RSC_API\s+[^;(]*?\b(rsc_\w+)\s*\(([^;]*?)\)\s*;", header, flags=re.S):
         args = m.group(2).strip()
         want[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return want
+
+
+def test_ctypes_signatures_match_the_header():
+    want = header_parameter_counts()
+    assert want, "no declarations parsed from the header"
+    mismatched = {k: (n, len(_lib.SIGNATURES[k][1])) for k, n in want.items()
+                  if len(_lib.SIGNATURES[k][1]) != n}
+    assert not mismatched, f"(header, ctypes) parameter counts differ: {mismatched}"
+
+
+def test_rust_binding_parameter_counts_match_the_header():
+    want = header_parameter_counts()
     ffi = (ROOT / "rust" / "rusticide-cuda" / "src" / "ffi.rs").read_text()
     got = {}
     for m in re.finditer(r"\bfn\s+(rsc_\w+)\s*\(([^)]*)\)", ffi, flags=re.S):
