@@ -28,3 +28,13 @@ def test_reference_arm_prints_one_json_line(oracle_lib):
     assert d["config"]["workload"] == "cfg0"
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference")
+
+
+def test_headline_profile_gives_the_roofline_traffic():
+    """roofline.traffic on the headline comes from the committed ncu summary's
+    dram_bytes_per_launch line; a launch reads each logit at least once."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    traffic = bench.committed_traffic("cfg2p")
+    assert traffic is not None
+    assert traffic >= 1024 * 151936 * 4
