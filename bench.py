@@ -200,9 +200,26 @@ def cpu_baseline(x_host, u_host, params, seconds: float, threads: int, greedy: b
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
+    # The same on one core (the reference samples one row per call on one
+    # thread): the first rows of the sample, for a quarter of the time.
+    n1 = max(1, x_host.shape[0] // max(threads, 1))
+    x1, u1 = x_host[:n1], u_host[:n1]
+    rows1 = 0
+    t1 = time.perf_counter()
+    while True:
+        if greedy:
+            O.greedy_rows(x1, threads=1)
+        else:
+            O.sample_rows(x1, op, u1, threads=1)
+        rows1 += n1
+        if time.perf_counter() - t1 >= seconds / 4:
+            break
+    dt1 = time.perf_counter() - t1
     return {"value": rows / dt, "unit": "rows/s", "cores": threads, "kind": "port",
             "sample": f"{x_host.shape[0]} rows x {x_host.shape[1]} of the workload, "
-                      f"{rows // x_host.shape[0]} passes, {dt:.1f} s, {threads} threads"}
+                      f"{rows // x_host.shape[0]} passes, {dt:.1f} s, {threads} threads",
+            "single_core_value": rows1 / dt1,
+            "single_core_sample": f"{n1} rows, {rows1 // n1} passes, {dt1:.1f} s, 1 thread"}
 
 
 def run_reference(args, cfg, rank: int, world: int) -> None:

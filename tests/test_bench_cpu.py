@@ -38,3 +38,18 @@ def test_headline_profile_gives_the_roofline_traffic():
     traffic = bench.committed_traffic("cfg2p")
     assert traffic is not None
     assert traffic >= 1024 * 151936 * 4
+
+
+def test_cpu_baseline_reports_all_cores_and_one_core(oracle_lib):
+    """The GPU arm's cpu_baseline (the oracle on the host cores) also carries a
+    single-core figure; both are positive rates over bounded samples."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from rusticide_b200 import SamplingParams, synth
+    x = synth.make_logits(16, 32000, base_seed=3)
+    u = synth.uniforms(16, seed=4)
+    out = bench.cpu_baseline(x, u, SamplingParams(0.8, 40, 0.95), 0.4, 4)
+    assert out["value"] > 0 and out["single_core_value"] > 0
+    assert out["cores"] == 4 and out["kind"] == "port" and out["unit"] == "rows/s"
+    g = bench.cpu_baseline(x, u, SamplingParams(0.0, 40, 0.95), 0.2, 2, greedy=True)
+    assert g["single_core_value"] > 0
