@@ -220,10 +220,12 @@ RSC_API rsc_status rsc_penalize(rsc_sampler *sampler, float *d_logits, size_t ro
                         float penalty, void *stream);
 
 /*
- * Seeds per-row generator states: state[r] = seeds[r] (device arrays), the
- * wyrand stream that fastrand::Rng::with_seed starts from
- * (src/sampler.rs:17-23). The stream's f32 conversion is restated from the
- * published generator and is unverified against fastrand 2.5.0 output.
+ * Seeds per-row generator states: state[r] = seeds[r] (device arrays), as
+ * fastrand::Rng::with_seed(seed) starts (src/sampler.rs:17-23). A row that
+ * draws takes fastrand's Rng::f32() from its state: wyrand with the wyhash
+ * v4.2 constants, then the low 32 bits' top 23 as a [1,2) mantissa, minus 1.
+ * Restated from fastrand 2.5.0's published source, not checked against the
+ * crate's own output (no Rust toolchain on this image).
  */
 RSC_API rsc_status rsc_rng_seed(const uint64_t *d_seeds, uint64_t *d_rng_states,
                         size_t rows, void *stream);
@@ -279,8 +281,9 @@ RSC_API rsc_status rsc_shard_merge(rsc_sampler *sampler, const void *d_records,
  * Its sorting scratch is a fixed array of RSC_NOALLOC_SCRATCH_BYTES inside the
  * library's device image. Every GPU that loads the library holds that array
  * until the process exits. vocab above RSC_NOALLOC_MAX_VOCAB returns
- * RSC_ERR_CAPACITY. The first call on a device looks the array's address up
- * (cudaGetSymbolAddress). Make that first call before any stream capture.
+ * RSC_ERR_CAPACITY, and vocab 0 with rows > 0 returns RSC_ERR_INVALID_SHAPE. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress). Make that first call before any stream capture;
+ * a set-up that failed is retried by the next call.
  * All calls on a device share the array. Calls whose kernels overlap on the
  * GPU (different streams with no ordering between them) race on it, so order
  * them on one stream or with events. Rows are sampled by the large-survivor

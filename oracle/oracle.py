@@ -68,6 +68,7 @@ def lib() -> ctypes.CDLL:
             "rso_pick": (None, [P, SZ, ctypes.POINTER(RsoParams), ctypes.c_float, ctypes.POINTER(RsoResult)]),
             "rso_filter": (SZ, [P, SZ, ctypes.POINTER(RsoParams), P, P]),
             "rso_topk_threshold": (ctypes.c_float, [P, SZ, ctypes.c_float, ctypes.c_uint32]),
+            "rso_topp_edge": (SZ, [P, SZ, ctypes.POINTER(RsoParams), _F, _F]),
             "rso_softmax": (None, [P, SZ, P]),
             "rso_argmax": (SZ, [P, SZ]),
             "rso_apply_repetition_penalty": (None, [P, SZ, P, SZ, ctypes.c_float]),
@@ -148,6 +149,14 @@ def filter_(logits, p: RsoParams) -> tuple[np.ndarray, np.ndarray]:
     val = np.empty(max(1, x.size), dtype=np.float32)
     n = lib().rso_filter(x.ctypes.data, x.size, ctypes.byref(p), idx.ctypes.data, val.ctypes.data)
     return idx[:n].copy(), val[:n].copy()
+
+
+def topp_edge(logits, p: RsoParams) -> tuple[int, float, float]:
+    """(kept count, running sum before, running sum after) at the top-p cut."""
+    x = _f32(logits)
+    b, a = ctypes.c_float(), ctypes.c_float()
+    n = lib().rso_topp_edge(x.ctypes.data, x.size, ctypes.byref(p), ctypes.byref(b), ctypes.byref(a))
+    return int(n), float(b.value), float(a.value)
 
 
 def topk_threshold(logits, temperature: float, k: int) -> float:

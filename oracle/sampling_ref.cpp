@@ -16,10 +16,15 @@
 #include "sampling_ref.h"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <condition_variable>
 #include <cstring>
+#include <functional>
 #include <limits>
+#include <mutex>
 #include <thread>
+#include <unistd.h>
 #include <utility>
 #include <vector>
 
@@ -85,8 +90,11 @@ std::vector<Entry> top_k(const float *logits, size_t n, float temperature,
     return entries;
 }
 
-// Candidates::top_p, candidates.rs:55-78
-void top_p(std::vector<Entry> &entries, float p) {
+// Candidates::top_p, candidates.rs:55-78. `before`/`after` (nullable) get
+// the running sum before and after the element that crossed p (both the
+// final sum when nothing crossed), for the benchmark's boundary counter.
+void top_p(std::vector<Entry> &entries, float p, float *before = nullptr,
+           float *after = nullptr) {
     std::sort(entries.begin(), entries.end(), [](const Entry &a, const Entry &b) {
         int32_t ka = total_key(a.value), kb = total_key(b.value);
         if (ka != kb) return ka > kb;  // b.1.total_cmp(&a.1)
@@ -99,15 +107,18 @@ void top_p(std::vector<Entry> &entries, float p) {
         exp_vals[i] = expf(entries[i].value - max);
     float exp_sum = 0.0f;  // fold(0.0, |sum, &value| sum + value)
     for (float v : exp_vals) exp_sum = exp_sum + v;
-    float cumsum = 0.0f;
+    float cumsum = 0.0f, prev = 0.0f;
     size_t cutoff = exp_vals.size();
     for (size_t i = 0; i < exp_vals.size(); ++i) {
+        prev = cumsum;
         cumsum += exp_vals[i] / exp_sum;
         if (cumsum > p) {
             cutoff = i + 1;
             break;
         }
     }
+    if (before) *before = cutoff == exp_vals.size() && !(cumsum > p) ? cumsum : prev;
+    if (after) *after = cumsum;
     entries.resize(cutoff);
     std::sort(entries.begin(), entries.end(),
               [](const Entry &a, const Entry &b) { return a.index < b.index; });
@@ -189,21 +200,108 @@ void reset(rso_result *out) {
     out->cdf_hi = std::numeric_limits<float>::quiet_NaN();
 }
 
+// A persistent pool of worker threads for the batched helpers: threads are
+// created on the first call that asks for them (or for a different count)
+// and then reused, so that timing a batch does not time thread creation.
+// Rows are handed out one at a time from a shared counter. One batch runs at
+// a time (calls are serialised by `call_mu`).
+class RowPool {
+  public:
+    static RowPool &get() {
+        static RowPool pool;
+        return pool;
+    }
+
+    void run(size_t rows, size_t threads, const std::function<void(size_t)> &f) {
+        std::lock_guard<std::mutex> call_lock(call_mu_);
+        if (owner_ != getpid()) {
+            // A forked child inherits the pool's bookkeeping but not its
+            // threads: forget them (never join) and start afresh.
+            for (auto *t : workers_) (void)t;  // leaked on purpose
+            workers_.clear();
+            owner_ = getpid();
+        }
+        resize(threads);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            job_ = &f;
+            rows_ = rows;
+            next_.store(0);
+            pending_ = workers_.size();
+            ++generation_;
+        }
+        cv_.notify_all();
+        std::unique_lock<std::mutex> lk(mu_);
+        done_cv_.wait(lk, [this] { return pending_ == 0; });
+        job_ = nullptr;
+    }
+
+    ~RowPool() {
+        if (owner_ == getpid()) resize(0);
+    }
+
+  private:
+    void resize(size_t n) {
+        if (n == workers_.size()) return;
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            stop_ = true;
+            ++generation_;
+        }
+        cv_.notify_all();
+        for (auto *t : workers_) {
+            t->join();
+            delete t;
+        }
+        workers_.clear();
+        uint64_t gen0;
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            stop_ = false;
+            gen0 = generation_;
+        }
+        // A worker starts from the generation current at its creation, so a
+        // batch posted before the thread first runs is still seen as new.
+        for (size_t w = 0; w < n; ++w) workers_.push_back(new std::thread([this, gen0] { loop(gen0); }));
+    }
+
+    void loop(uint64_t seen) {
+        while (true) {
+            const std::function<void(size_t)> *job;
+            size_t rows;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return stop_ || generation_ != seen; });
+                if (stop_) return;
+                seen = generation_;
+                job = job_;
+                rows = rows_;
+            }
+            for (size_t r = next_.fetch_add(1); r < rows; r = next_.fetch_add(1)) (*job)(r);
+            std::lock_guard<std::mutex> lk(mu_);
+            if (--pending_ == 0) done_cv_.notify_all();
+        }
+    }
+
+    std::mutex call_mu_, mu_;
+    std::condition_variable cv_, done_cv_;
+    std::vector<std::thread *> workers_;
+    pid_t owner_ = getpid();
+    const std::function<void(size_t)> *job_ = nullptr;
+    size_t rows_ = 0, pending_ = 0;
+    std::atomic<size_t> next_{0};
+    uint64_t generation_ = 0;
+    bool stop_ = false;
+};
+
 template <typename F>
 void parallel_rows(size_t rows, int threads, F f) {
     if (threads <= 1 || rows < 2) {
         for (size_t r = 0; r < rows; ++r) f(r);
         return;
     }
-    size_t t = std::min<size_t>(static_cast<size_t>(threads), rows);
-    std::vector<std::thread> pool;
-    pool.reserve(t);
-    for (size_t w = 0; w < t; ++w) {
-        pool.emplace_back([=, &f]() {
-            for (size_t r = w; r < rows; r += t) f(r);
-        });
-    }
-    for (auto &th : pool) th.join();
+    const std::function<void(size_t)> job = f;
+    RowPool::get().run(rows, static_cast<size_t>(threads), job);
 }
 
 }  // namespace
@@ -289,6 +387,15 @@ size_t rso_filter(const float *logits, size_t n, const rso_params *params,
     return c.size();
 }
 
+size_t rso_topp_edge(const float *logits, size_t n, const rso_params *params,
+                     float *before, float *after) {
+    std::vector<Entry> c = top_k(logits, n, params->temperature, params->top_k);
+    *before = *after = std::numeric_limits<float>::quiet_NaN();
+    if (!(params->top_p < 1.0f)) return c.size();
+    top_p(c, params->top_p, before, after);
+    return c.size();
+}
+
 float rso_topk_threshold(const float *logits, size_t n, float temperature,
                          uint32_t k32) {
     size_t k = k32;
@@ -346,19 +453,23 @@ void rso_sample_with_temp_rows(const float *logits, size_t rows, size_t n,
     });
 }
 
-// wyrand (Wang Yi, public domain): state += 0xa0761d6478bd642f; the output is
-// the xor of the two halves of the 128-bit product state * (state ^
-// 0xe7037ed1a0b428db). UNVERIFIED as the fastrand 2.5.0 stream.
+// fastrand::Rng::gen_u64 (fastrand 2.5.0, Cargo.lock:191-195; called through
+// Rng::f32 at src/sampler.rs:112): wyrand with the final wyhash v4.2
+// constants, as fastrand's lib.rs has them since its 2.1 release. The state
+// advances by 0x2d358dccaa6c78a5; the output is the xor of the two halves of
+// the 128-bit product state * (state ^ 0x8bb84b93962eacc9). Restated from the
+// crate's published source, not checked against the crate's own output.
 uint64_t rso_rng_next_u64(uint64_t *state) {
-    uint64_t s = *state + 0xa0761d6478bd642fULL;
+    uint64_t s = *state + 0x2d358dccaa6c78a5ULL;
     *state = s;
     unsigned __int128 t = static_cast<unsigned __int128>(s) *
-                          static_cast<unsigned __int128>(s ^ 0xe7037ed1a0b428dbULL);
+                          static_cast<unsigned __int128>(s ^ 0x8bb84b93962eacc9ULL);
     return static_cast<uint64_t>(t) ^ static_cast<uint64_t>(t >> 64);
 }
 
-// A uniform in [0, 1): the top 23 bits of the low 32-bit word fill the
-// mantissa of a float in [1, 2), then 1.0 is subtracted. UNVERIFIED.
+// fastrand::Rng::f32: gen_u32 is the low 32 bits of gen_u64; its top 23 bits
+// fill the mantissa of a float in [1, 2) (bits (1 << 30) - (1 << 23) +
+// (x >> 9)), and 1.0 is subtracted.
 float rso_rng_f32(uint64_t *state) {
     uint32_t x = static_cast<uint32_t>(rso_rng_next_u64(state));
     uint32_t bits = 0x3F800000u | (x >> 9);

@@ -11,11 +11,11 @@
  * is what Rust's f32::exp calls on x86_64-unknown-linux-gnu.
  *
  * The reference's seeded generator (the fastrand 2.5.0 crate, absent from the
- * reference tree) is not restated bit-for-bit here as a pinned fact: every
- * draw takes the uniform `u` the caller supplies, and reports whether a draw
- * was consumed. rso_rng_* below is a restatement of the published wyrand
- * generator with a [1,2)-mantissa f32 conversion; it is UNVERIFIED against the
- * crate because no Rust toolchain exists on this image.
+ * reference tree): every draw takes the uniform `u` the caller supplies, and
+ * reports whether a draw was consumed. rso_rng_* below restate fastrand's
+ * published Rng::gen_u64 (wyrand with the wyhash v4.2 constants) and Rng::f32;
+ * the restatement is not checked against the crate's own output, because no
+ * Rust toolchain exists on this image.
  */
 #ifndef RUSTICIDE_SAMPLING_ORACLE_H
 #define RUSTICIDE_SAMPLING_ORACLE_H
@@ -81,6 +81,14 @@ void rso_pick(const float *logits, size_t n, const rso_params *params, float u,
 size_t rso_filter(const float *logits, size_t n, const rso_params *params,
                   uint32_t *out_index, float *out_value);
 
+/* Candidates::top_p's cut-off on one row (src/candidates.rs:55-78), for the
+ * benchmark's boundary counter: *before and *after get the running sum before
+ * and after the element whose cumulative mass first exceeded top_p (both the
+ * final sum when none did; NaN when top-p is off). Returns the size of the
+ * kept set. */
+size_t rso_topp_edge(const float *logits, size_t n, const rso_params *params,
+                     float *before, float *after);
+
 /* kth_largest on the scaled row, src/candidates.rs:38-43,93-97; returns -inf
  * when top-k is disabled (k == 0 or k >= n). */
 float rso_topk_threshold(const float *logits, size_t n, float temperature,
@@ -110,7 +118,7 @@ void rso_sample_with_temp_rows(const float *logits, size_t rows, size_t n,
                                size_t row_stride, float temperature,
                                const float *u, rso_result *out, int threads);
 
-/* wyrand restatement (UNVERIFIED against fastrand 2.5.0, see header). */
+/* fastrand::Rng::gen_u64 and Rng::f32, restated (see the header comment). */
 uint64_t rso_rng_next_u64(uint64_t *state);
 float rso_rng_f32(uint64_t *state);
 

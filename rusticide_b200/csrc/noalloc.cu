@@ -18,12 +18,13 @@
 // Limits: the array holds RSC_NOALLOC_SCRATCH_BYTES; a call needs
 // 16 * vocab bytes per concurrently sampled row, so vocab is at most
 // RSC_NOALLOC_SCRATCH_BYTES / 16 and larger vocabularies are rejected with
-// RSC_ERR_CAPACITY. Every call on a device shares the one array, so calls
-// whose kernels overlap on the GPU (different streams, no ordering between
-// them) race on it; order them on one stream or with events.
+// RSC_ERR_CAPACITY; vocab 0 with rows > 0 is RSC_ERR_INVALID_SHAPE. Every
+// call on a device shares the one array, so calls whose kernels overlap on
+// the GPU (different streams, no ordering between them) race on it; order
+// them on one stream or with events.
 #include <cuda_runtime.h>
 
-#include <atomic>
+#include <cmath>
 #include <mutex>
 
 #include "rsc_kernels.h"
@@ -37,8 +38,8 @@ constexpr size_t kMaxDevices = 64;
 static __device__ __align__(256) uint32_t kNoAllocScratch[kScratchWords];
 
 struct DeviceSetup {
-    std::once_flag once;
-    cudaError_t status = cudaErrorNotReady;
+    std::mutex mu;
+    bool ready = false;           // set only by a set-up that succeeded
     uint32_t *scratch = nullptr;  // device address of kNoAllocScratch
     int num_sms = 0;
 };
@@ -47,18 +48,24 @@ DeviceSetup g_setup[kMaxDevices];
 
 // Set-up of `device`, which must be current: the device address of the
 // scratch array (a host-side reference to the symbol is not a device
-// address) and the SM count.
-DeviceSetup *setup_device(int device) {
+// address) and the SM count. Only a successful set-up is kept; after a
+// failure (for example a first call made inside a stream capture) the next
+// call tries again.
+cudaError_t setup_device(int device, DeviceSetup **out) {
     DeviceSetup *s = &g_setup[device];
-    std::call_once(s->once, [s, device]() {
+    std::lock_guard<std::mutex> lock(s->mu);
+    if (!s->ready) {
         void *ptr = nullptr;
+        int sms = 0;
         cudaError_t e = cudaGetSymbolAddress(&ptr, kNoAllocScratch);
-        if (e == cudaSuccess)
-            e = cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, device);
-        if (e == cudaSuccess) s->scratch = static_cast<uint32_t *>(ptr);
-        s->status = e;
-    });
-    return s;
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess || !ptr || sms <= 0) return e != cudaSuccess ? e : cudaErrorUnknown;
+        s->scratch = static_cast<uint32_t *>(ptr);
+        s->num_sms = sms;
+        s->ready = true;
+    }
+    *out = s;
+    return cudaSuccess;
 }
 
 }  // namespace
@@ -73,6 +80,7 @@ extern "C" RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t r
     if (vocab > RSC_NOALLOC_MAX_VOCAB) return RSC_ERR_CAPACITY;
     if (rows > 0 && vocab > 0 && row_stride < vocab) return RSC_ERR_INVALID_SHAPE;
     if (rows == 0) return RSC_OK;
+    if (vocab == 0) return RSC_ERR_INVALID_SHAPE;
     if (!d_out_ids || !d_out_status || (vocab > 0 && !d_logits)) return RSC_ERR_INVALID_ARGUMENT;
     if ((reinterpret_cast<uintptr_t>(d_logits) & 3u) != 0) return RSC_ERR_INVALID_ARGUMENT;
     const bool argmax = params->temperature == 0.0f || params->top_k == 1;
@@ -81,8 +89,8 @@ extern "C" RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t r
     int device = -1;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0) return RSC_ERR_NO_DEVICE;
     if (static_cast<size_t>(device) >= kMaxDevices) return RSC_ERR_NO_DEVICE;
-    DeviceSetup *s = setup_device(device);
-    if (s->status != cudaSuccess || !s->scratch) return RSC_ERR_CUDA;
+    DeviceSetup *s = nullptr;
+    if (setup_device(device, &s) != cudaSuccess) return RSC_ERR_CUDA;
 
     rsc::CallParams cp;
     cp.temperature = params->temperature;
@@ -92,7 +100,9 @@ extern "C" RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t r
     cp.topk_active = params->top_k != 0 && static_cast<size_t>(params->top_k) < vocab;
     cp.topp_active = params->top_p < 1.0f;
     cp.argmax_branch = argmax;
-    cp.normal_scale = false;  // unused by the large-survivor kernel
+    // As rsc_sample derives it: it sends rows with no filter at a normal scale
+    // to the large kernel's filter-free branch, with the same results.
+    cp.normal_scale = std::isfinite(cp.scale) && cp.scale > 0.0f;
     cp.mode = rsc::kModeSampleLogits;
     cp.uniforms = d_uniforms;
     cp.rng_states = d_rng_states;
@@ -101,7 +111,7 @@ extern "C" RSC_API rsc_status rsc_sample_noalloc(const float *d_logits, size_t r
     cp.surv_cap = 0;
 
     // Rows sampled at once: kLargeCtasPerSm per SM, as many as the scratch holds.
-    const size_t per_row = 4 * (vocab > 0 ? vocab : 1);
+    const size_t per_row = 4 * vocab;
     size_t slots = kScratchWords / per_row;
     const size_t resident = static_cast<size_t>(s->num_sms) * rsc::kLargeCtasPerSm;
     if (slots > resident) slots = resident;

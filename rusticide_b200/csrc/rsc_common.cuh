@@ -110,6 +110,12 @@ __device__ __forceinline__ void load_exp_table(double *dst) {
 }
 
 // The method's core for x in [-104, 88.72...] (no range checks).
+// Attribution: the reduction constant, the 2^(j/32) table and the three
+// polynomial coefficients below are the published data of Arm's
+// optimized-routines expf (math/expf.c with math/exp2f_data.c, Copyright
+// Arm Limited, MIT licence, later MIT OR Apache-2.0 WITH LLVM-exception);
+// glibc ships the same data in sysdeps/ieee754/flt-32/e_exp2f_data.c. The
+// code around them is this library's own restatement of the method.
 __device__ __forceinline__ float expf_core(float x, const double *tab) {
     const double kInvLn2N = 0x1.71547652b82fep+0 * 32.0;
     const double kShift = 0x1.8p+52;
@@ -143,16 +149,25 @@ __device__ __forceinline__ float expf_ref(float x, const double *tab) {
 }
 
 // ---------------------------------------------------------------------------
-// Per-row generator: the published wyrand step (Wang Yi, public domain) and a
-// uniform in [0,1) from the top 23 bits of the low 32-bit word placed in the
-// mantissa of a float in [1,2), minus 1. This is the stream
-// fastrand::Rng::with_seed(seed) is documented to follow; it is unverified
-// against fastrand 2.5.0 because no Rust toolchain exists on this image.
+// Per-row generator: fastrand::Rng as the reference's Sampler uses it
+// (Rng::with_seed(seed), then f32(); crates/rusticide-sampling/src/
+// sampler.rs:17-23,112; fastrand 2.5.0 per Cargo.lock:191-195).
+//  - gen_u64 is the wyrand step with the final wyhash v4.2 constants, which
+//    fastrand's lib.rs uses since its 2.1 release: the state advances by
+//    0x2d358dccaa6c78a5, and the output is the xor of the two halves of the
+//    128-bit product s * (s ^ 0x8bb84b93962eacc9).
+//  - f32 takes gen_u32 (the low 32 bits of gen_u64), keeps its top 23 bits
+//    as the mantissa of a float in [1, 2) and subtracts 1.
+// The stream is restated from the crate's published source; it is not
+// checked against output of the crate itself (no Rust toolchain here).
 // ---------------------------------------------------------------------------
+constexpr uint64_t kWyInc = 0x2d358dccaa6c78a5ULL;
+constexpr uint64_t kWyXor = 0x8bb84b93962eacc9ULL;
+
 __host__ __device__ __forceinline__ uint64_t wyrand_next(uint64_t *state) {
-    uint64_t s = *state + 0xa0761d6478bd642fULL;
+    uint64_t s = *state + kWyInc;
     *state = s;
-    uint64_t b = s ^ 0xe7037ed1a0b428dbULL;
+    uint64_t b = s ^ kWyXor;
 #ifdef __CUDA_ARCH__
     uint64_t hi = __umul64hi(s, b);
 #else

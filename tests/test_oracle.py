@@ -85,6 +85,58 @@ def test_rng_stream_is_deterministic_and_uniform(oracle_lib):
     assert abs(float(a.mean()) - 0.5) < 0.05
 
 
+# First three draws of fastrand::Rng::with_seed(seed) for seeds 0, 1 and 42
+# (the reference's Sampler::new, src/sampler.rs:17-23, and rng.f32() at
+# src/sampler.rs:112; fastrand 2.5.0 per Cargo.lock:191-195). Derived by hand
+# from the crate's published lib.rs, restated in _fastrand_f32 below:
+#   gen_u64: s = state + 0x2d358dccaa6c78a5 (mod 2^64); state = s;
+#            t = s * (s ^ 0x8bb84b93962eacc9) as u128; out = lo64(t) ^ hi64(t)
+#   f32:     bits = (1 << 30) - (1 << 23) + (lo32(out) >> 9); f = bits - 1.0
+# Each entry is (gen_u64 output, f32 bits before the subtraction, the draw).
+_h = float.fromhex
+FASTRAND_KATS = {
+    0: [(0x9a45cd888d59f0d6, 0x3fc6acf8, _h("0x1.1ab3ep-1")),
+        (0x01445b6a189663f5, 0x3f8c4b31, _h("0x1.89662p-4")),
+        (0x1842218b97e7a496, 0x3fcbf3d2, _h("0x1.2fcf48p-1"))],
+    1: [(0xa833bdcdb6d1beb1, 0x3fdb68df, _h("0x1.6da37cp-1")),
+        (0x88dc97e5aab5fe3d, 0x3fd55aff, _h("0x1.556bfcp-1")),
+        (0x3d58bb03f31a4686, 0x3ff98d23, _h("0x1.e6348cp-1"))],
+    42: [(0xca71d87c76983989, 0x3fbb4c1c, _h("0x1.da60ep-2")),
+         (0x7e5ba61552085fc6, 0x3fa9042f, _h("0x1.482178p-2")),
+         (0xcdf101e3bab88b9f, 0x3fdd5c45, _h("0x1.757114p-1"))],
+}
+
+
+def _fastrand_f32(state: int) -> tuple[int, int, int, float]:
+    """One Rng::f32() step in exact integer arithmetic: (new state, gen_u64
+    output, f32 bits in [1, 2), the draw)."""
+    m = (1 << 64) - 1
+    s = (state + 0x2D358DCCAA6C78A5) & m
+    t = s * (s ^ 0x8BB84B93962EACC9)
+    out = ((t & m) ^ (t >> 64)) & m
+    bits = (1 << 30) - (1 << 23) + ((out & 0xFFFFFFFF) >> 9)
+    f = float(np.array([bits], dtype=np.uint32).view(np.float32)[0]) - 1.0
+    return s, out, bits, f
+
+
+def test_fastrand_draws_match_the_published_algorithm(oracle_lib):
+    import ctypes
+    L = oracle_lib.lib()
+    for seed, want in FASTRAND_KATS.items():
+        st_py = seed
+        st_u = ctypes.c_uint64(seed)
+        st_f = ctypes.c_uint64(seed)
+        for out, bits, draw in want:
+            st_py, out_py, bits_py, f_py = _fastrand_f32(st_py)
+            assert (out_py, bits_py, f_py) == (out, bits, draw)
+            assert L.rso_rng_next_u64(ctypes.byref(st_u)) == out
+            got = L.rso_rng_f32(ctypes.byref(st_f))
+            assert np.float32(got) == np.float32(draw)
+        assert st_u.value == st_f.value == st_py
+        assert np.array_equal(oracle_lib.rng_stream(seed, 3),
+                              np.array([w[2] for w in want], dtype=np.float32))
+
+
 def test_expf_is_glibc(oracle_lib):
     x = np.linspace(-104, 0, 10001, dtype=np.float32)
     y = oracle_lib.expf(x)
