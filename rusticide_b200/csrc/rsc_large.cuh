@@ -20,10 +20,12 @@
 //  4. argmax (last maximum) or the draw: the exact index-order running sum of
 //     the probabilities, stopping at the first r < cumsum
 //     (sampler.rs:111-121), falling back to the last survivor.
-// The sums use block_replay, which reproduces the sequential binary32 loop
+// The sums use block_replay2, which reproduces the sequential binary32 loop
 // bit for bit. Rows without any filter take plain_row, which needs no
 // threshold, sort or scratch.
 #pragma once
+
+#include <type_traits>
 
 #include "rsc_block.cuh"
 #include "rsc_kernels.h"
@@ -35,20 +37,51 @@ constexpr int kItems = 4;
 constexpr int kBatch = 8;  // loads in flight per thread in the row passes
 
 // Shared memory of the large-row code for a block of T threads.
+#ifndef RSC_REPLAY_ITEMS
+#define RSC_REPLAY_ITEMS 8
+#endif
+constexpr int kReplayItems = RSC_REPLAY_ITEMS;
+constexpr int kReplayRaw = 8;  // positions per thread per round of the compacting replay
+
 template <int T>
 struct LargeSmem {
     double exp_tab[32];
-    ReplaySmem rs;
     uint32_t hist[256];
     uint32_t sel[2];
     uint32_t red32[32];
     unsigned long long red64[32];
     float redf[32];
-    uint32_t wcount[T / 32][256];
-    uint32_t base[256];
-    uint32_t tile_total[256];
     uint32_t bcast[4];
+    union {
+        struct {  // the radix sort's per-warp digit counts
+            uint32_t wcount[T / 32][256];
+            uint32_t base[256];
+            uint32_t tile_total[256];
+        };
+        // The replays (never live with the sorts): the compacting form for
+        // the large kernel's blocks, the plain form in the streaming
+        // kernel's smaller epilogue workspace.
+        typename std::conditional<(T >= 512), Replay3Smem<T, kReplayItems, kReplayRaw>,
+                                  Replay2Smem<T, kReplayItems>>::type rs;
+        uint32_t dbucket[T >= 512 ? 8192 : 4096];  // the distance sort's buckets
+    };
 };
+
+// Buckets of the distance sort for a block of T threads, and the largest
+// bucket it sorts (a row with a larger one takes the radix sort).
+template <int T>
+constexpr uint32_t kDBuckets = T >= 512 ? 8192u : 4096u;
+constexpr uint32_t kDMaxBucket = 512;
+
+// The exact replay of a large-row block of T threads.
+template <int T, typename Term, typename Pred>
+__device__ __forceinline__ ReplayResult row_replay(uint32_t n, Term &term, Pred pred,
+                                                   LargeSmem<T> &sm) {
+    if constexpr (T >= 512)
+        return block_replay3<T, kReplayItems, kReplayRaw>(n, term, pred, sm.rs);
+    else
+        return block_replay2<T, kReplayItems>(n, term, pred, sm.rs);
+}
 
 struct RowView {
     const float *p;
@@ -78,6 +111,9 @@ struct ExpTerm {
     bool divide;
     const double *tab;
     float vthr;
+    const float *raw;  // load_at(j) reads raw[j] (for L2 prefetch), or null
+
+    __device__ const float *raw_ptr() const { return raw; }
 
     __device__ void prepare(float tmin) {
         const bool ok = tmin >= 0x1p-100f && fabsf(mx) < kPosInf &&
@@ -95,11 +131,39 @@ struct ExpTerm {
 
 template <typename Load, typename Keep>
 __device__ __forceinline__ ExpTerm<Load, Keep> exp_term(Load load, Keep keep, float mx, float div,
-                                                        bool divide, const double *tab) {
-    return ExpTerm<Load, Keep>{load, keep, mx, div, divide, tab, kNegInf};
+                                                        bool divide, const double *tab,
+                                                        const float *raw = nullptr) {
+    return ExpTerm<Load, Keep>{load, keep, mx, div, divide, tab, kNegInf, raw};
 }
 
-constexpr int kReplayItems = 8;
+// Terms read from an array of precomputed exp values (+0 or a negative value
+// marks a position that takes no part): t[j], or fl(t[j] / div). prepare
+// drops terms certainly below tmin: t < tmin, or t < tmin * div * (1 - 2^-20)
+// for the quotient (within an ulp of t / div).
+template <typename Keep>
+struct ArrayTerm {
+    const float *t;
+    Keep keep;  // (j, t) -> whether position j takes part (t >= 0 already checked)
+    float div;
+    bool divide;
+    float thr;
+
+    __device__ const float *raw_ptr() const { return t; }
+    __device__ void prepare(float tmin) {
+        thr = divide ? (div > 0.0f && div < kPosInf ? tmin * div * (1.0f - 0x1p-20f) : 0.0f) : tmin;
+    }
+    __device__ float load(uint32_t j) const { return t[j]; }
+    __device__ float eval(uint32_t j, float v) const {
+        if (!(v >= 0.0f) || v < thr || !keep(j, v)) return 0.0f;
+        return divide ? __fdiv_rn(v, div) : v;
+    }
+};
+
+template <typename Keep>
+__device__ __forceinline__ ArrayTerm<Keep> array_term(const float *t, Keep keep, float div,
+                                                      bool divide) {
+    return ArrayTerm<Keep>{t, keep, div, divide, 0.0f};
+}
 
 // Stable LSD radix sort (4 passes of 8 bits) of n (key, idx) pairs by key
 // ascending, ping-ponging between (ka, ia) and (kb, ib); the result ends in
@@ -282,9 +346,8 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
     auto not_neg_inf = [](uint32_t, float v) { return v != kNegInf; };
     if (valid) {
         // softmax sum (filters.rs:7-8), from -0.0 (the row is not empty).
-        auto s_term = exp_term(row_value, not_neg_inf, mx, 1.0f, false, tab);
-        const float sum = block_replay<T, kReplayItems>(n, s_term, [](float) { return false; },
-                                                               sm.rs).sum;
+        auto s_term = exp_term(row_value, not_neg_inf, mx, 1.0f, false, tab, rv.p);
+        const float sum = row_replay<T>(n, s_term, [](float) { return false; }, sm).sum;
         const bool norm = (fabsf(sum) < kPosInf) && sum > 0.0f;
         uint32_t pos;
         int32_t flags = RSC_ROW_FLAG_LARGE_PATH;
@@ -295,9 +358,9 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
             __syncthreads();
             const float r = __uint_as_float(sm.bcast[0]);
             __syncthreads();
-            auto p_term = exp_term(row_value, not_neg_inf, mx, sum, norm, tab);
-            ReplayResult dr = block_replay<T, kReplayItems>(
-                n, p_term, [r](float c) { return r < c; }, sm.rs);
+            auto p_term = exp_term(row_value, not_neg_inf, mx, sum, norm, tab, rv.p);
+            ReplayResult dr = row_replay<T>(
+                n, p_term, [r](float c) { return r < c; }, sm);
             float lo, hi;
             if (dr.stop >= 0) {
                 pos = static_cast<uint32_t>(dr.stop);
@@ -322,6 +385,335 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
     __syncthreads();
 }
 
+// The distance sort of the top-p step. The reference sorts the survivors by
+// value, descending, with ties by index (candidates.rs:56-57), and its sums
+// then add exp(v - max) in that order (candidates.rs:62-75). Here the sort
+// key is the distance d = fl(max - v) >= 0 instead:
+//  - d is non-increasing in v, and elements with equal d have equal terms
+//    exp(-d) = exp(fl(v - max)), so the running sums over d ascending equal
+//    the reference's sums over value descending;
+//  - which elements a cut-off keeps is decided on d, and only inside the
+//    group of elements that share the cut-off's d (contiguous in the
+//    reference's order) does the reference's (value, index) order matter.
+// The sort itself: a histogram of d over kDBuckets linear buckets (d >= 104,
+// whose term is +0, all in the last bucket), a scatter into the buckets, and
+// within each bucket a rank count (the last bucket keeps any order: its
+// terms are all +0, and a cut-off never falls on a +0 term).
+__device__ __forceinline__ uint32_t dist_bucket(float d, float inv, uint32_t nb) {
+    if (!(d < 104.0f)) return nb - 1u;
+    return min(__float2uint_rz(__fmul_rn(d, inv)), nb - 2u);
+}
+
+// Sampler::sample_logits on a row with top-p on and a finite surviving set
+// (src/sampler.rs:44-54; Candidates::filter, candidates.rs:16-78; softmax,
+// filters.rs:5-15; the draw, sampler.rs:111-121), through the distance sort
+// above. Scratch: S1 and S2 (n words each) for the sort, and E (n floats):
+// E[i] = exp(fl(v_i - max)) for a survivor of top-k, -1 otherwise. Each
+// term is computed once: the sorted sums read S2 (the same values in the
+// reference's order), the index-order sums read E.
+// Returns false, having written no output, when the row does not qualify
+// (a NaN or infinite survivor, no survivor, or a bucket above kDMaxBucket);
+// the caller then samples it with large_row's radix sort.
+template <int T>
+__device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t row, float thr,
+                              uint32_t *scratch, uint32_t *out_ids, int32_t *out_status,
+                              float *out_probs, LargeSmem<T> &sm) {
+    const uint32_t n = rv.n;
+    uint32_t *S1 = scratch, *S2 = scratch + n;
+    float *E = reinterpret_cast<float *>(scratch + 2 * static_cast<size_t>(n));
+    const double *tab = sm.exp_tab;
+    constexpr uint32_t NB = kDBuckets<T>;
+
+    // A: the survivors' maximum, minimum and count, and whether any is NaN
+    // or infinite.
+    float smax = kNegInf, smin = kPosInf;
+    uint32_t nsurv = 0, odd = 0;
+    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {  // loads first, all in flight together
+            const uint32_t i = i0 + q * T + threadIdx.x;
+            v[q] = i < n ? rv.value(i) : kNegInf;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            if (survives(v[q], thr)) {
+                ++nsurv;
+                if (!(fabsf(v[q]) < kPosInf)) odd = 1;
+                smax = fmaxf(smax, v[q]);
+                smin = fminf(smin, v[q]);
+            }
+        }
+    }
+    smax = block_reduce<T>(smax, sm.redf, OpFMax());
+    smin = -block_reduce<T>(-smin, sm.redf, OpFMax());
+    nsurv = block_reduce<T>(nsurv, sm.red32, OpAddU32());
+    odd = block_reduce<T>(odd, sm.red32, OpOrU32());
+    if (nsurv == 0 || odd) return false;
+    const float span = fminf(__fsub_rn(smax, smin), 104.0f);
+    const float inv = span > 0.0f ? __fdiv_rn(static_cast<float>(NB - 1), span) : 0.0f;
+
+    // B: histogram of the buckets of d = fl(max - v).
+    for (uint32_t b = threadIdx.x; b < NB; b += T) sm.dbucket[b] = 0;
+    __syncthreads();
+    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const uint32_t i = i0 + q * T + threadIdx.x;
+            v[q] = i < n ? rv.value(i) : kNegInf;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q)
+            if (survives(v[q], thr))
+                atomicAdd(&sm.dbucket[dist_bucket(__fsub_rn(smax, v[q]), inv, NB)], 1u);
+    }
+    __syncthreads();
+    // The largest sorted bucket decides; then the exclusive prefix. Thread t
+    // owns buckets [t * kPer, (t + 1) * kPer) (T need not divide NB).
+    constexpr uint32_t kPer = (NB + T - 1) / T;
+    uint32_t tot = 0, big = 0;
+    for (uint32_t e = 0; e < kPer; ++e) {
+        const uint32_t b = threadIdx.x * kPer + e;
+        if (b >= NB) break;
+        const uint32_t c = sm.dbucket[b];
+        tot += c;
+        if (b < NB - 1) big = max(big, c);
+    }
+    big = block_reduce<T>(big, sm.red32, OpMaxU32());
+    if (big > kDMaxBucket) return false;
+    {
+        uint32_t all;
+        uint32_t run = block_exclusive_add<T>(tot, sm.red32, &all);
+        for (uint32_t e = 0; e < kPer; ++e) {
+            const uint32_t b = threadIdx.x * kPer + e;
+            if (b >= NB) break;
+            const uint32_t c = sm.dbucket[b];
+            sm.dbucket[b] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+
+    // C: the terms, once: E in index order, and S1 in bucket order (the
+    // order inside a bucket is the scatter's). After it, dbucket[b] is the
+    // end of bucket b.
+    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const uint32_t i = i0 + q * T + threadIdx.x;
+            v[q] = i < n ? rv.value(i) : kNegInf;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const uint32_t i = i0 + q * T + threadIdx.x;
+            if (i < n) {
+                float t = -1.0f;
+                if (survives(v[q], thr)) {
+                    const float d = __fsub_rn(smax, v[q]);
+                    // exp(v - max) of the reference: fl(v - max) = -d exactly.
+                    t = expf_ref(-d, tab);
+                    const uint32_t pos = atomicAdd(&sm.dbucket[dist_bucket(d, inv, NB)], 1u);
+                    S1[pos] = __float_as_uint(t);
+                }
+                E[i] = t;
+            }
+        }
+    }
+    __syncthreads();
+
+    // D: each bucket in order of its terms, descending (t >= 0: the bit
+    // patterns order like the values; equal terms keep the scatter order,
+    // and any order of equal terms gives the reference's sums). A bucket
+    // holds an interval of d, so the whole array is in the reference's order
+    // of terms. The last bucket (d >= 104, every term +0) keeps any order.
+    for (uint32_t q0 = 0; q0 < nsurv; q0 += T) {
+        const uint32_t q = q0 + threadIdx.x;
+        if (q < nsurv) {
+            const uint32_t tb = S1[q];
+            // The bucket of position q: the last bucket whose start is <= q.
+            // Found by binary search over the bucket ends.
+            uint32_t lo = 0, hi = NB - 1;
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (sm.dbucket[mid] > q) hi = mid;
+                else lo = mid + 1;
+            }
+            const uint32_t b = lo;
+            const uint32_t st = b ? sm.dbucket[b - 1] : 0u, en = sm.dbucket[b];
+            uint32_t rank = q - st;
+            if (b < NB - 1) {
+                rank = 0;
+                for (uint32_t r = st; r < en; ++r) {
+                    const uint32_t o = S1[r];
+                    rank += (o > tb || (o == tb && r < q)) ? 1u : 0u;
+                }
+            }
+            S2[st + rank] = tb;
+        }
+    }
+    __syncthreads();
+
+    // E, F: exp_sum and the cut-off over the sorted terms (candidates.rs:62-75).
+    const float *sorted = reinterpret_cast<const float *>(S2);
+    auto all = [](uint32_t, float) { return true; };
+    auto es_term = array_term(sorted, all, 1.0f, false);
+    const float exp_sum = row_replay<T>(nsurv, es_term, [](float) { return false; }, sm).sum;
+    const float p = cp.top_p;
+    auto cs_term = array_term(sorted, all, exp_sum, true);
+    const ReplayResult cs = row_replay<T>(nsurv, cs_term, [p](float x) { return x > p; }, sm);
+    bool cut = false, gsplit = false;
+    float tc = 0.0f;
+    uint32_t cut_key = 0, cut_idx = 0;
+    if (cs.stop >= 0 && static_cast<uint32_t>(cs.stop) + 1 < nsurv) {
+        cut = true;
+        const uint32_t c = static_cast<uint32_t>(cs.stop);
+        tc = sorted[c];
+        // The group of terms equal to the cut-off's: how many of it precede
+        // the cut-off, and its size. Only inside it does the reference's
+        // (value desc, index asc) order decide who is kept.
+        uint32_t above = 0, eq = 0;
+        for (uint32_t q0 = 0; q0 < nsurv; q0 += T) {
+            const uint32_t q = q0 + threadIdx.x;
+            if (q < nsurv) {
+                const float o = sorted[q];
+                above += o > tc ? 1u : 0u;
+                eq += o == tc ? 1u : 0u;
+            }
+        }
+        above = block_reduce<T>(above, sm.red32, OpAddU32());
+        eq = block_reduce<T>(eq, sm.red32, OpAddU32());
+        const uint32_t m = c - above + 1u;
+        if (m < eq) {
+            // The group's first m in the reference's order: gather it (S1 and
+            // S2 are free now), rank it, and take the m-th.
+            gsplit = true;
+            if (threadIdx.x == 0) sm.bcast[1] = 0;
+            __syncthreads();
+            uint32_t *gk = S1, *gi = S2;
+            for (uint32_t i0 = 0; i0 < n; i0 += T) {
+                const uint32_t i = i0 + threadIdx.x;
+                if (i < n && E[i] == tc) {
+                    const uint32_t at = atomicAdd(&sm.bcast[1], 1u);
+                    gk[at] = total_key(rv.value(i));
+                    gi[at] = i;
+                }
+            }
+            __syncthreads();
+            const uint32_t gn = sm.bcast[1];
+            for (uint32_t a = threadIdx.x; a < gn; a += T) {
+                uint32_t rank = 0;
+                for (uint32_t b = 0; b < gn; ++b)
+                    rank += (gk[b] > gk[a] || (gk[b] == gk[a] && gi[b] < gi[a])) ? 1u : 0u;
+                if (rank + 1u == m) {
+                    sm.bcast[2] = gk[a];
+                    sm.bcast[3] = gi[a];
+                }
+            }
+            __syncthreads();
+            cut_key = sm.bcast[2];
+            cut_idx = sm.bcast[3];
+            __syncthreads();
+        }
+    }
+    // Kept after top-p: E[i] >= 0 (a top-k survivor) and at or before the
+    // cut-off in the reference's order.
+    auto kept = [&](uint32_t i, float e) {
+        if (!(e >= 0.0f)) return false;
+        if (!cut || e > tc) return true;
+        if (e < tc) return false;
+        if (!gsplit) return true;
+        const uint32_t k = total_key(rv.value(i));
+        return k > cut_key || (k == cut_key && i <= cut_idx);
+    };
+
+    // G: the last kept position (sample_multinomial's fallback).
+    uint32_t last = 0;
+    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
+        float e[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const uint32_t i = i0 + q * T + threadIdx.x;
+            e[q] = i < n ? E[i] : -1.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+            const uint32_t i = i0 + q * T + threadIdx.x;
+            if (kept(i, e[q])) last = max(last, i);
+        }
+    }
+    last = block_reduce<T>(last, sm.red32, OpMaxU32());
+
+    // H: the softmax sum in index order (filters.rs:7-8); its maximum is the
+    // row's (the largest survivor is always kept), so its terms are E.
+    auto s_term = array_term(E, kept, 1.0f, false);
+    const float sum = row_replay<T>(n, s_term, [](float) { return false; }, sm).sum;
+    // sum >= 1 (the maximum's own term), finite: normalise.
+
+    // Optional survivor outputs (as large_row).
+    if (cp.out_nsurv || cp.out_surv || cp.out_survp) {
+        uint32_t written = 0;
+        constexpr uint32_t kTile = T * kItems;
+        for (uint32_t t0 = 0; t0 < n; t0 += kTile) {
+            uint32_t cnt = 0;
+            bool keep[kItems];
+#pragma unroll
+            for (int q = 0; q < kItems; ++q) {
+                const uint32_t i = t0 + threadIdx.x * kItems + q;
+                keep[q] = i < n && kept(i, E[i]);
+                cnt += keep[q] ? 1u : 0u;
+            }
+            uint32_t total;
+            uint32_t off = block_exclusive_add<T>(cnt, sm.red32, &total);
+            if (cp.out_surv || cp.out_survp) {
+#pragma unroll
+                for (int q = 0; q < kItems; ++q) {
+                    if (keep[q]) {
+                        const uint32_t i = t0 + threadIdx.x * kItems + q;
+                        if (written + off < cp.surv_cap) {
+                            const size_t at = row * cp.surv_cap + written + off;
+                            if (cp.out_surv) cp.out_surv[at] = i;
+                            if (cp.out_survp) cp.out_survp[at] = __fdiv_rn(E[i], sum);
+                        }
+                        ++off;
+                    }
+                }
+            }
+            written += total;
+        }
+        if (cp.out_nsurv && threadIdx.x == 0) cp.out_nsurv[row] = written;
+        __syncthreads();
+    }
+
+    // I: the draw (sampler.rs:111-121).
+    if (threadIdx.x == 0) sm.bcast[0] = __float_as_uint(row_uniform(cp, row));
+    __syncthreads();
+    const float r = __uint_as_float(sm.bcast[0]);
+    __syncthreads();
+    auto p_term = array_term(E, kept, sum, true);
+    const ReplayResult dr = row_replay<T>(n, p_term, [r](float x) { return r < x; }, sm);
+    uint32_t pos;
+    float lo, hi;
+    if (dr.stop >= 0) {
+        pos = static_cast<uint32_t>(dr.stop);
+        lo = dr.before;
+        hi = dr.after;
+    } else {
+        pos = last;
+        lo = hi = dr.sum;
+    }
+    int32_t status = RSC_ROW_OK | RSC_ROW_FLAG_LARGE_PATH;
+    if (fabsf(r - hi) < 1e-6f || fabsf(r - lo) < 1e-6f) status |= RSC_ROW_FLAG_DRAW_NEAR_BOUNDARY;
+    if (threadIdx.x == 0) {
+        out_ids[row] = pos;
+        out_status[row] = status;
+        if (out_probs) out_probs[row] = __fdiv_rn(E[pos], sum);
+    }
+    __syncthreads();
+    return true;
+}
+
 template <int T>
 __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, uint32_t *scratch,
                           uint32_t *out_ids, int32_t *out_status, float *out_probs,
@@ -337,6 +729,9 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
         thr = key_to_float(kth);
     }
     auto in_topk = [&](uint32_t i, float v) { return with_temp || survives(v, thr); };
+    if (!with_temp && cp.topp_active && !cp.argmax_branch &&
+        topp_dist_row<T>(cp, rv, row, thr, scratch, out_ids, out_status, out_probs, sm))
+        return;
 
     // --- top-p (candidates.rs:55-78) --------------------------------------------
     bool cut = false;
@@ -385,13 +780,11 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
             auto sorted_value = [&](uint32_t j) { return key_to_float(~ka[j]); };
             auto all = [](uint32_t, float) { return true; };
             auto es_term = exp_term(sorted_value, all, maxv, 1.0f, false, tab);
-            ReplayResult es = block_replay<T, kReplayItems>(
-                ns, es_term, [](float) { return false; }, sm.rs);
+            ReplayResult es = row_replay<T>(ns, es_term, [](float) { return false; }, sm);
             const float exp_sum = es.sum;
             const float p = cp.top_p;
             auto cs_term = exp_term(sorted_value, all, maxv, exp_sum, true, tab);
-            ReplayResult cs = block_replay<T, kReplayItems>(
-                ns, cs_term, [p](float s) { return s > p; }, sm.rs);
+            ReplayResult cs = row_replay<T>(ns, cs_term, [p](float x) { return x > p; }, sm);
             if (cs.stop >= 0 && static_cast<uint32_t>(cs.stop) + 1 < ns) {
                 cut = true;
                 cut_key = ~ka[cs.stop];
@@ -441,7 +834,7 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
     float sum = -0.0f;
     if (any) {
         auto s_term = exp_term(row_value, survivor, mx, 1.0f, false, tab);
-        sum = block_replay<T, kReplayItems>(n, s_term, [](float) { return false; }, sm.rs).sum;
+        sum = row_replay<T>(n, s_term, [](float) { return false; }, sm).sum;
     }
     const bool norm = (fabsf(sum) < kPosInf) && sum > 0.0f;
 
@@ -507,8 +900,8 @@ __device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, u
             const float r = __uint_as_float(sm.bcast[0]);
             __syncthreads();
             auto p_term = exp_term(row_value, survivor, mx, sum, norm, tab);
-            ReplayResult dr = block_replay<T, kReplayItems>(
-                n, p_term, [r](float c) { return r < c; }, sm.rs);
+            ReplayResult dr = row_replay<T>(
+                n, p_term, [r](float c) { return r < c; }, sm);
             float lo, hi;
             if (dr.stop >= 0) {
                 pos = static_cast<uint32_t>(dr.stop);
