@@ -64,6 +64,14 @@ struct LargeSmem {
         typename std::conditional<(T >= 512), Replay3Smem<T, kReplayItems, kReplayRaw>,
                                   Replay2Smem<T, kReplayItems>>::type rs;
         uint32_t dbucket[T >= 512 ? 8192 : 4096];  // the distance sort's buckets
+        Replay2Smem<T, kReplayItems> rs2;           // replays over a relevant-term list
+        struct {
+            uint32_t cmax[1024];  // plain rows: chunk maxima (total keys), then bounds
+            // A round of the list, staged for coalesced stores (large blocks
+            // only: the streaming kernel's epilogue workspace is smaller).
+            float stage_t[T >= 512 ? T * 16 : 1];
+            uint32_t stage_i[T >= 512 ? T * 16 : 1];
+        };
     };
 };
 
@@ -274,23 +282,44 @@ __device__ void block_radix_sort(uint32_t *ka, uint32_t *ia, uint32_t *kb, uint3
 // Rows with no filter: sample_logits with top_k = 0 and top_p >= 1 at a
 // normal scale, and sample_with_temp. Every logit that is not -inf survives
 // (sample_with_temp keeps -inf too, whose term is +0 all the same), so the row
-// needs no threshold, no sort and no survivor test beyond v != -inf:
-//  1. one pass for the maximum, the last survivor and (argmax branch) the
-//     last maximum, with 128-bit loads;
-//  2. the exact index-order sum of exp(v - max) (filters.rs:5-15);
-//  3. the draw: the exact running sum of the probabilities up to the first
-//     r < cumsum (sampler.rs:111-121).
+// needs no threshold and no sort:
+//  1. one pass (128-bit loads) for the maximum, the last survivor, the
+//     argmax branch's last maximum, and the maximum of each chunk of the row;
+//  2. one pass that lists, in order, the positions whose term can change a
+//     running sum, with their terms exp(v - max). The running sum before
+//     position j is at least the largest term before it, which is at least
+//     the largest term of the chunks before j's chunk, T_c; a term at most
+//     T_c * 2^-27 is below half a spacing of the softmax sum there, and of
+//     the draw's running sum of probabilities (each divided by the sum), so
+//     it rounds away in both and is left out: v_j < max(chunks before) -
+//     18.75 (27 ln 2 = 18.715, plus the rounding of the exps and of v - max);
+//  3. the exact index-order sum of the listed terms (filters.rs:5-15);
+//  4. the draw: the exact running sum of the listed probabilities up to the
+//     first r < cumsum (sampler.rs:111-121), else the last survivor.
+// Scratch: the list, 2 * n words.
 template <int T>
-__device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, uint32_t *out_ids,
-                          int32_t *out_status, float *out_probs, LargeSmem<T> &sm) {
+__device__ __noinline__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, uint32_t *scratch,
+                          uint32_t *out_ids, int32_t *out_status, float *out_probs,
+                          LargeSmem<T> &sm) {
+    constexpr uint32_t kMaxChunks = 1024;
     const uint32_t n = rv.n;
     const bool with_temp = rv.with_temp;
     const bool want_amax = !with_temp && cp.argmax_branch;
+    // Chunks of whole rounds of the first pass (T * kBatch float4) past the
+    // scalar head; at most kMaxChunks of them.
+    constexpr uint32_t kRound = T * kBatch * 4u;
+    const uint32_t chunk = max(1u, (n + kMaxChunks * kRound - 1) / (kMaxChunks * kRound)) * kRound;
+    for (uint32_t c = threadIdx.x; c < kMaxChunks; c += T) sm.cmax[c] = kKeyNegInf;
+    __syncthreads();
     float mx = kNegInf;
     uint32_t last = 0;
     unsigned long long amax = 0;
-    auto visit = [&](float x, uint32_t i) {
-        const float v = rv.scaled(x);
+    const uint32_t mis = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(rv.p) >> 2) & 3u);
+    const uint32_t head = mis ? min(n, 4u - mis) : 0u;
+    const uint32_t n4 = (n - head) / 4u;
+    const uint32_t tail0 = head + 4u * n4;
+    auto chunk_of = [&](uint32_t i) { return i < head ? 0u : min((i - head) / chunk, kMaxChunks - 1); };
+    auto visit = [&](float v, uint32_t i) {
         mx = fmaxf(mx, v);
         last = (v != kNegInf && i > last) ? i : last;
         if (want_amax && v != kNegInf) {
@@ -299,14 +328,19 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
         }
     };
     // Scalar head up to a 16-byte boundary, float4 body, scalar tail.
-    const uint32_t mis = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(rv.p) >> 2) & 3u);
-    const uint32_t head = mis ? min(n, 4u - mis) : 0u;
-    const uint32_t n4 = (n - head) / 4u;
-    const uint32_t tail0 = head + 4u * n4;
-    if (threadIdx.x < head) visit(rv.p[threadIdx.x], threadIdx.x);
-    if (threadIdx.x >= 32 && threadIdx.x - 32 < n - tail0)
-        visit(rv.p[tail0 + threadIdx.x - 32], tail0 + threadIdx.x - 32);
+    if (threadIdx.x < head) {
+        const float v = rv.value(threadIdx.x);
+        visit(v, threadIdx.x);
+        atomicMax(&sm.cmax[0], total_key(v));
+    }
+    if (threadIdx.x >= 32 && threadIdx.x - 32 < n - tail0) {
+        const uint32_t i = tail0 + threadIdx.x - 32;
+        const float v = rv.value(i);
+        visit(v, i);
+        atomicMax(&sm.cmax[chunk_of(i)], total_key(v));
+    }
     const float4 *p4 = reinterpret_cast<const float4 *>(rv.p + head);
+    const uint32_t lane = threadIdx.x & 31u;
     for (uint32_t q0 = 0; q0 < n4; q0 += T * kBatch) {
         float4 f[kBatch];
 #pragma unroll
@@ -314,17 +348,24 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
             const uint32_t q = q0 + b * T + threadIdx.x;
             f[b] = q < n4 ? p4[q] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
         }
+        float gm = kNegInf;
 #pragma unroll
         for (int b = 0; b < kBatch; ++b) {
             const uint32_t q = q0 + b * T + threadIdx.x;
             if (q < n4) {
                 const uint32_t i = head + 4u * q;
-                visit(f[b].x, i);
-                visit(f[b].y, i + 1);
-                visit(f[b].z, i + 2);
-                visit(f[b].w, i + 3);
+                const float v0 = rv.scaled(f[b].x), v1 = rv.scaled(f[b].y);
+                const float v2 = rv.scaled(f[b].z), v3 = rv.scaled(f[b].w);
+                visit(v0, i);
+                visit(v1, i + 1);
+                visit(v2, i + 2);
+                visit(v3, i + 3);
+                gm = fmaxf(gm, fmaxf(fmaxf(v0, v1), fmaxf(v2, v3)));
             }
         }
+        // A round lies in one chunk (chunk is a whole number of rounds).
+        gm = warp_max(gm);
+        if (lane == 0) atomicMax(&sm.cmax[(4u * q0) / chunk], total_key(gm));
     }
     mx = block_reduce<T>(mx, sm.redf, OpFMax());
     last = block_reduce<T>(last, sm.red32, OpMaxU32());
@@ -342,12 +383,134 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
     uint32_t token = 0;
     float prob = __uint_as_float(0x7fc00000u);
     const double *tab = sm.exp_tab;
-    auto row_value = [&](uint32_t i) { return rv.value(i); };
-    auto not_neg_inf = [](uint32_t, float v) { return v != kNegInf; };
     if (valid) {
+        // Exclusive prefix maximum of the chunk maxima, as the leave-out
+        // bound of each chunk: v < bound is left out.
+        if (threadIdx.x < 32) {
+            constexpr uint32_t kPer = kMaxChunks / 32;
+            uint32_t m = kKeyNegInf;
+            for (uint32_t e = 0; e < kPer; ++e) m = max(m, sm.cmax[lane * kPer + e]);
+            uint32_t incl = m;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl = max(incl, v);
+            }
+            uint32_t run = __shfl_up_sync(0xffffffffu, incl, 1);
+            if (lane == 0) run = kKeyNegInf;
+            __syncwarp();
+            for (uint32_t e = 0; e < kPer; ++e) {
+                const uint32_t ce = sm.cmax[lane * kPer + e];
+                const float pm = key_to_float(run);
+                // No chunk before: every logit is listed.
+                sm.cmax[lane * kPer + e] =
+                    __float_as_uint(pm == kNegInf ? kNegInf : __fsub_rn(pm, 18.75f));
+                run = max(run, ce);
+            }
+        }
+        __syncthreads();
+        // The list of terms that can matter, in index order.
+        float *lt = reinterpret_cast<float *>(scratch);
+        uint32_t *li = scratch + n;
+        uint32_t cnt = 0;
+        auto listed = [&](float v, uint32_t i) {
+            return v != kNegInf && !(v < __uint_as_float(sm.cmax[chunk_of(i)]));
+        };
+        if (head > 0) {
+            // The head, in order, by the first lanes.
+            const float v = threadIdx.x < head ? rv.value(threadIdx.x) : kNegInf;
+            const bool k = threadIdx.x < head && listed(v, threadIdx.x);
+            const uint32_t bal = __ballot_sync(0xffffffffu, k);
+            if (threadIdx.x < 32 && k) {
+                const uint32_t at = __popc(bal & ((1u << lane) - 1u));
+                lt[at] = expf_ref(__fsub_rn(v, mx), tab);
+                li[at] = threadIdx.x;
+            }
+            if (threadIdx.x < 32) sm.bcast[1] = __popc(bal);
+            __syncthreads();
+            cnt = sm.bcast[1];
+            __syncthreads();
+        }
+        // The body, each thread a run of kListBatch consecutive float4 (one
+        // chunk: a chunk is a multiple of the run).
+        constexpr int kListBatch = 4;
+        for (uint32_t q0 = 0; q0 < n4; q0 += T * kListBatch) {
+            float4 f[kListBatch];
+            const uint32_t qt = q0 + threadIdx.x * kListBatch;
+#pragma unroll
+            for (int b = 0; b < kListBatch; ++b)
+                f[b] = qt + b < n4 ? p4[qt + b] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+            const float bound = __uint_as_float(sm.cmax[min((4u * qt) / chunk, kMaxChunks - 1)]);
+            uint32_t mine = 0;
+#pragma unroll
+            for (int b = 0; b < kListBatch; ++b) {
+                f[b] = make_float4(rv.scaled(f[b].x), rv.scaled(f[b].y), rv.scaled(f[b].z),
+                                   rv.scaled(f[b].w));
+                mine += (f[b].x != kNegInf && !(f[b].x < bound)) ? 1u : 0u;
+                mine += (f[b].y != kNegInf && !(f[b].y < bound)) ? 1u : 0u;
+                mine += (f[b].z != kNegInf && !(f[b].z < bound)) ? 1u : 0u;
+                mine += (f[b].w != kNegInf && !(f[b].w < bound)) ? 1u : 0u;
+            }
+            // The next round into L2 meanwhile: one 128-byte line per thread.
+            if (q0 + T * kListBatch + 8u * threadIdx.x < n4)
+                prefetch_l2(p4 + q0 + T * kListBatch + 8u * threadIdx.x);
+            uint32_t total;
+            uint32_t at = block_exclusive_add<T>(mine, sm.red32, &total);
+            constexpr bool kStage = T >= 512;
+            if (!kStage) at += cnt;
+            if (mine) {
+                // Staged in shared memory, then stored in order, coalesced.
+#pragma unroll
+                for (int b = 0; b < kListBatch; ++b) {
+                    const uint32_t i = head + 4u * (qt + b);
+                    const float v[4] = {f[b].x, f[b].y, f[b].z, f[b].w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (v[c] != kNegInf && !(v[c] < bound)) {
+                            const float t = expf_ref(__fsub_rn(v[c], mx), tab);
+                            if (kStage) {
+                                sm.stage_t[at] = t;
+                                sm.stage_i[at] = i + c;
+                            } else {
+                                lt[at] = t;
+                                li[at] = i + c;
+                            }
+                            ++at;
+                        }
+                    }
+                }
+            }
+            if (kStage) {
+                __syncthreads();
+                for (uint32_t e = threadIdx.x; e < total; e += T) {
+                    lt[cnt + e] = sm.stage_t[e];
+                    li[cnt + e] = sm.stage_i[e];
+                }
+                __syncthreads();
+            }
+            cnt += total;
+        }
+        if (tail0 < n) {
+            const uint32_t i = tail0 + threadIdx.x;
+            const float v = threadIdx.x < n - tail0 ? rv.value(i) : kNegInf;
+            const bool k = threadIdx.x < n - tail0 && listed(v, i);
+            const uint32_t bal = __ballot_sync(0xffffffffu, k);
+            if (threadIdx.x < 32 && k) {
+                const uint32_t at = cnt + __popc(bal & ((1u << lane) - 1u));
+                lt[at] = expf_ref(__fsub_rn(v, mx), tab);
+                li[at] = i;
+            }
+            if (threadIdx.x < 32) sm.bcast[1] = __popc(bal);
+            __syncthreads();
+            cnt += sm.bcast[1];
+            __syncthreads();
+        }
+        __syncthreads();
+        auto all = [](uint32_t, float) { return true; };
         // softmax sum (filters.rs:7-8), from -0.0 (the row is not empty).
-        auto s_term = exp_term(row_value, not_neg_inf, mx, 1.0f, false, tab, rv.p);
-        const float sum = row_replay<T>(n, s_term, [](float) { return false; }, sm).sum;
+        auto s_term = array_term(lt, all, 1.0f, false);
+        const float sum =
+            block_replay2<T, kReplayItems>(cnt, s_term, [](float) { return false; }, sm.rs2).sum;
         const bool norm = (fabsf(sum) < kPosInf) && sum > 0.0f;
         uint32_t pos;
         int32_t flags = RSC_ROW_FLAG_LARGE_PATH;
@@ -358,12 +521,12 @@ __device__ void plain_row(const CallParams &cp, const RowView &rv, size_t row, u
             __syncthreads();
             const float r = __uint_as_float(sm.bcast[0]);
             __syncthreads();
-            auto p_term = exp_term(row_value, not_neg_inf, mx, sum, norm, tab, rv.p);
-            ReplayResult dr = row_replay<T>(
-                n, p_term, [r](float c) { return r < c; }, sm);
+            auto p_term = array_term(lt, all, sum, norm);
+            ReplayResult dr = block_replay2<T, kReplayItems>(
+                cnt, p_term, [r](float c) { return r < c; }, sm.rs2);
             float lo, hi;
             if (dr.stop >= 0) {
-                pos = static_cast<uint32_t>(dr.stop);
+                pos = li[dr.stop];
                 lo = dr.before;
                 hi = dr.after;
             } else {
@@ -404,10 +567,45 @@ __device__ __forceinline__ uint32_t dist_bucket(float d, float inv, uint32_t nb)
     return min(__float2uint_rz(__fmul_rn(d, inv)), nb - 2u);
 }
 
+// Calls f(v, i) for every position i of the row, v its scaled logit, in no
+// particular order: a scalar head up to a 16-byte boundary, a float4 body with
+// kB loads per thread in flight, a scalar tail.
+template <int T, int kB = 4, typename F>
+__device__ __forceinline__ void for_each_scaled(const RowView &rv, F f) {
+    const uint32_t n = rv.n;
+    const uint32_t mis = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(rv.p) >> 2) & 3u);
+    const uint32_t head = mis ? min(n, 4u - mis) : 0u;
+    const uint32_t n4 = (n - head) / 4u;
+    const uint32_t tail0 = head + 4u * n4;
+    if (threadIdx.x < head) f(rv.value(threadIdx.x), threadIdx.x);
+    if (threadIdx.x >= 32 && threadIdx.x - 32 < n - tail0)
+        f(rv.value(tail0 + threadIdx.x - 32), tail0 + threadIdx.x - 32);
+    const float4 *p4 = reinterpret_cast<const float4 *>(rv.p + head);
+    for (uint32_t q0 = 0; q0 < n4; q0 += T * kB) {
+        float4 x[kB];
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {  // loads first, all in flight together
+            const uint32_t q = q0 + b * T + threadIdx.x;
+            if (q < n4) x[b] = p4[q];
+        }
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+            const uint32_t q = q0 + b * T + threadIdx.x;
+            if (q < n4) {
+                const uint32_t i = head + 4u * q;
+                f(rv.scaled(x[b].x), i);
+                f(rv.scaled(x[b].y), i + 1);
+                f(rv.scaled(x[b].z), i + 2);
+                f(rv.scaled(x[b].w), i + 3);
+            }
+        }
+    }
+}
+
 // Sampler::sample_logits on a row with top-p on and a finite surviving set
 // (src/sampler.rs:44-54; Candidates::filter, candidates.rs:16-78; softmax,
 // filters.rs:5-15; the draw, sampler.rs:111-121), through the distance sort
-// above. Scratch: S1 and S2 (n words each) for the sort, and E (n floats):
+// above. Scratch: S1, S2 and SB (n words each) for the sort, and E (n floats):
 // E[i] = exp(fl(v_i - max)) for a survivor of top-k, -1 otherwise. Each
 // term is computed once: the sorted sums read S2 (the same values in the
 // reference's order), the index-order sums read E.
@@ -415,12 +613,13 @@ __device__ __forceinline__ uint32_t dist_bucket(float d, float inv, uint32_t nb)
 // (a NaN or infinite survivor, no survivor, or a bucket above kDMaxBucket);
 // the caller then samples it with large_row's radix sort.
 template <int T>
-__device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t row, float thr,
+__device__ __noinline__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t row, float thr,
                               uint32_t *scratch, uint32_t *out_ids, int32_t *out_status,
                               float *out_probs, LargeSmem<T> &sm) {
     const uint32_t n = rv.n;
     uint32_t *S1 = scratch, *S2 = scratch + n;
     float *E = reinterpret_cast<float *>(scratch + 2 * static_cast<size_t>(n));
+    uint32_t *SB = scratch + 3 * static_cast<size_t>(n);  // bucket of each S1 entry
     const double *tab = sm.exp_tab;
     constexpr uint32_t NB = kDBuckets<T>;
 
@@ -428,23 +627,14 @@ __device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t ro
     // or infinite.
     float smax = kNegInf, smin = kPosInf;
     uint32_t nsurv = 0, odd = 0;
-    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {  // loads first, all in flight together
-            const uint32_t i = i0 + q * T + threadIdx.x;
-            v[q] = i < n ? rv.value(i) : kNegInf;
+    for_each_scaled<T>(rv, [&](float v, uint32_t) {
+        if (survives(v, thr)) {
+            ++nsurv;
+            if (!(fabsf(v) < kPosInf)) odd = 1;
+            smax = fmaxf(smax, v);
+            smin = fminf(smin, v);
         }
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            if (survives(v[q], thr)) {
-                ++nsurv;
-                if (!(fabsf(v[q]) < kPosInf)) odd = 1;
-                smax = fmaxf(smax, v[q]);
-                smin = fminf(smin, v[q]);
-            }
-        }
-    }
+    });
     smax = block_reduce<T>(smax, sm.redf, OpFMax());
     smin = -block_reduce<T>(-smin, sm.redf, OpFMax());
     nsurv = block_reduce<T>(nsurv, sm.red32, OpAddU32());
@@ -456,18 +646,9 @@ __device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t ro
     // B: histogram of the buckets of d = fl(max - v).
     for (uint32_t b = threadIdx.x; b < NB; b += T) sm.dbucket[b] = 0;
     __syncthreads();
-    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            const uint32_t i = i0 + q * T + threadIdx.x;
-            v[q] = i < n ? rv.value(i) : kNegInf;
-        }
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q)
-            if (survives(v[q], thr))
-                atomicAdd(&sm.dbucket[dist_bucket(__fsub_rn(smax, v[q]), inv, NB)], 1u);
-    }
+    for_each_scaled<T>(rv, [&](float v, uint32_t) {
+        if (survives(v, thr)) atomicAdd(&sm.dbucket[dist_bucket(__fsub_rn(smax, v), inv, NB)], 1u);
+    });
     __syncthreads();
     // The largest sorted bucket decides; then the exclusive prefix. Thread t
     // owns buckets [t * kPer, (t + 1) * kPer) (T need not divide NB).
@@ -498,29 +679,19 @@ __device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t ro
     // C: the terms, once: E in index order, and S1 in bucket order (the
     // order inside a bucket is the scatter's). After it, dbucket[b] is the
     // end of bucket b.
-    for (uint32_t i0 = 0; i0 < n; i0 += T * kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            const uint32_t i = i0 + q * T + threadIdx.x;
-            v[q] = i < n ? rv.value(i) : kNegInf;
+    for_each_scaled<T>(rv, [&](float v, uint32_t i) {
+        float t = -1.0f;
+        if (survives(v, thr)) {
+            const float d = __fsub_rn(smax, v);
+            // exp(v - max) of the reference: fl(v - max) = -d exactly.
+            t = expf_ref(-d, tab);
+            const uint32_t b = dist_bucket(d, inv, NB);
+            const uint32_t pos = atomicAdd(&sm.dbucket[b], 1u);
+            S1[pos] = __float_as_uint(t);
+            SB[pos] = b;
         }
-#pragma unroll
-        for (int q = 0; q < kBatch; ++q) {
-            const uint32_t i = i0 + q * T + threadIdx.x;
-            if (i < n) {
-                float t = -1.0f;
-                if (survives(v[q], thr)) {
-                    const float d = __fsub_rn(smax, v[q]);
-                    // exp(v - max) of the reference: fl(v - max) = -d exactly.
-                    t = expf_ref(-d, tab);
-                    const uint32_t pos = atomicAdd(&sm.dbucket[dist_bucket(d, inv, NB)], 1u);
-                    S1[pos] = __float_as_uint(t);
-                }
-                E[i] = t;
-            }
-        }
-    }
+        E[i] = t;
+    });
     __syncthreads();
 
     // D: each bucket in order of its terms, descending (t >= 0: the bit
@@ -532,15 +703,7 @@ __device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t ro
         const uint32_t q = q0 + threadIdx.x;
         if (q < nsurv) {
             const uint32_t tb = S1[q];
-            // The bucket of position q: the last bucket whose start is <= q.
-            // Found by binary search over the bucket ends.
-            uint32_t lo = 0, hi = NB - 1;
-            while (lo < hi) {
-                const uint32_t mid = (lo + hi) >> 1;
-                if (sm.dbucket[mid] > q) hi = mid;
-                else lo = mid + 1;
-            }
-            const uint32_t b = lo;
+            const uint32_t b = SB[q];
             const uint32_t st = b ? sm.dbucket[b - 1] : 0u, en = sm.dbucket[b];
             uint32_t rank = q - st;
             if (b < NB - 1) {
@@ -715,7 +878,7 @@ __device__ bool topp_dist_row(const CallParams &cp, const RowView &rv, size_t ro
 }
 
 template <int T>
-__device__ void large_row(const CallParams &cp, const RowView &rv, size_t row, uint32_t *scratch,
+__device__ __noinline__ void large_row(const CallParams &cp, const RowView &rv, size_t row, uint32_t *scratch,
                           uint32_t *out_ids, int32_t *out_status, float *out_probs,
                           LargeSmem<T> &sm) {
     const uint32_t n = rv.n;
@@ -940,7 +1103,7 @@ __device__ void sample_row(const CallParams &cp, const float *p, uint32_t vocab,
     RowView rv{p, vocab, cp.scale, cp.mode == kModeSampleWithTemp};
     const bool plain = !cp.out_nsurv && !cp.out_surv && !cp.out_survp &&
                        (rv.with_temp || (cp.normal_scale && !cp.topk_active && !cp.topp_active));
-    if (plain) plain_row<T>(cp, rv, row, out_ids, out_status, out_probs, sm);
+    if (plain) plain_row<T>(cp, rv, row, scratch, out_ids, out_status, out_probs, sm);
     else large_row<T>(cp, rv, row, scratch, out_ids, out_status, out_probs, sm);
 }
 
