@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define RSC_ABI_VERSION 1
+#define RSC_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define RSC_API __attribute__((visibility("default")))
@@ -147,12 +147,31 @@ RSC_API rsc_status rsc_sample_rows(rsc_sampler *sampler, const float *d_logits, 
  *                 the same survivors, the vector the reference's softmax
  *                 returns for the row (src/filters.rs:5-15, as
  *                 src/sampler.rs:50 computes it); entry i belongs to id i.
+ *
+ * Log-probabilities over the whole vocabulary (ABI 2; no reference
+ * counterpart: the reference's softmax normalises over the survivors only).
+ * With v the row's scaled logits as the reference's Candidates hold them
+ * (x * (1/T) for T > 0, x for T == 0, NaN read as -inf;
+ * src/candidates.rs:25-37):
+ * d_row_logsumexp  f32 per row, nullable: log(sum_j exp(v_j)) over the row
+ *                  (-inf when every v_j is -inf);
+ * d_token_logprob  f32 per row, nullable: v_token - logsumexp for the chosen
+ *                  token (NaN on a row whose status is not RSC_ROW_OK);
+ * d_survivor_logprobs rows x survivor_cap f32, nullable (needs
+ *                  d_survivor_ids): v_id - logsumexp for the listed survivors.
+ * They are computed with the fast binary32 exp and logf: within about 1e-6
+ * relative of the exact value, not bit-exact. On the streaming path the
+ * log-sum-exp is accumulated in the same pass over the logits; other rows
+ * take one more pass.
  */
 typedef struct {
     uint32_t *d_n_survivors;
     uint32_t *d_survivor_ids;
     size_t survivor_cap;
     float *d_survivor_probs;
+    float *d_row_logsumexp;
+    float *d_token_logprob;
+    float *d_survivor_logprobs;
 } rsc_sample_extras;
 
 /* rsc_sample with optional extra outputs (extras may be NULL). */

@@ -6,7 +6,7 @@
 
 use std::ffi::{c_char, c_int, c_void};
 
-pub(crate) const RSC_ABI_VERSION: c_int = 1;
+pub(crate) const RSC_ABI_VERSION: c_int = 2;
 
 pub(crate) const RSC_OK: c_int = 0;
 pub(crate) const RSC_ERR_INVALID_SHAPE: c_int = 2;
@@ -38,6 +38,9 @@ pub(crate) struct RscSampleExtras {
     pub(crate) d_survivor_ids: *mut u32,
     pub(crate) survivor_cap: usize,
     pub(crate) d_survivor_probs: *mut f32,
+    pub(crate) d_row_logsumexp: *mut f32,
+    pub(crate) d_token_logprob: *mut f32,
+    pub(crate) d_survivor_logprobs: *mut f32,
 }
 
 /// Opaque `rsc_sampler`.

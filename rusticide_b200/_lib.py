@@ -55,6 +55,9 @@ class RscSampleExtras(ctypes.Structure):
         ("d_survivor_ids", ctypes.c_void_p),
         ("survivor_cap", ctypes.c_size_t),
         ("d_survivor_probs", ctypes.c_void_p),
+        ("d_row_logsumexp", ctypes.c_void_p),
+        ("d_token_logprob", ctypes.c_void_p),
+        ("d_survivor_logprobs", ctypes.c_void_p),
     ]
 
 

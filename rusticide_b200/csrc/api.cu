@@ -33,6 +33,7 @@ struct rsc_sampler {
     void *lm_records = nullptr;       // [kLmheadMaxParts][max_rows] LM-head records (on first use)
     uint32_t *lm_error = nullptr;     // timeout flag of the LM-head kernel
     uint32_t *row_arrivals = nullptr; // [max_rows], zero between calls
+    uint2 *lse_parts = nullptr;       // [max_rows][kStreamMaxSplits] log-sum-exp parts (on first use)
     // Device staging of rsc_pick_host.
     float *stage_logits = nullptr;
     float *stage_uniforms = nullptr;
@@ -115,6 +116,7 @@ rsc::CallParams rows_from(const rsc::CallParams &cp, size_t r0) {
     if (b.out_surv) b.out_surv += r0 * b.surv_cap;
     if (b.out_survp) b.out_survp += r0 * b.surv_cap;
     if (b.row_params) b.row_params += r0;
+    if (b.lse_parts) b.lse_parts += r0 * b.lse_stride;
     return b;
 }
 
@@ -122,14 +124,19 @@ rsc_status stream_impl(rsc_sampler *s, const float *logits, size_t rows, uint32_
                        size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
                        int32_t *status, float *probs, cudaStream_t stream);
 
+// Whether a call's rows go to the streaming kernel (else the large kernel).
+bool streams_rows(const rsc::CallParams &cp, size_t vocab) {
+    return cp.mode == rsc::kModeSampleLogits && cp.normal_scale &&
+           ((cp.topk_active && cp.top_k <= rsc::kTwoPassTopK) ||
+            (!cp.topk_active && vocab <= rsc::kSmallCap));
+}
+
 rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t vocab,
                        size_t row_stride, const rsc::CallParams &cp, uint32_t *ids,
                        int32_t *status, float *probs, cudaStream_t stream) {
     if (rows == 0) return RSC_OK;
     const uint32_t v = static_cast<uint32_t>(vocab);
-    const bool small = cp.mode == rsc::kModeSampleLogits && cp.normal_scale &&
-                       ((cp.topk_active && cp.top_k <= rsc::kTwoPassTopK) ||
-                        (!cp.topk_active && vocab <= rsc::kSmallCap));
+    const bool small = streams_rows(cp, vocab);
     cudaError_t e;
     if (small) return stream_impl(s, logits, rows, v, row_stride, cp, ids, status, probs, stream);
     e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
@@ -262,6 +269,7 @@ rsc_status rsc_sampler_destroy(rsc_sampler *s) {
     cudaFree(s->lm_records);
     cudaFree(s->lm_error);
     cudaFree(s->row_arrivals);
+    cudaFree(s->lse_parts);
     cudaFree(s->stage_logits);
     cudaFree(s->stage_uniforms);
     cudaFree(s->stage_ids);
@@ -288,18 +296,50 @@ rsc_status rsc_sample_ex(rsc_sampler *s, const float *d_logits, size_t rows, siz
     if (!params || (rows > 0 && (!d_out_ids || !d_out_status))) return RSC_ERR_INVALID_ARGUMENT;
     rsc::CallParams cp = make_params(*params, vocab, d_uniforms, d_rng_states);
     if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    const bool want_lp = extras && (extras->d_row_logsumexp || extras->d_token_logprob ||
+                                    extras->d_survivor_logprobs);
     if (extras) {
-        if ((extras->d_survivor_ids || extras->d_survivor_probs) &&
+        if ((extras->d_survivor_ids || extras->d_survivor_probs || extras->d_survivor_logprobs) &&
             (extras->survivor_cap == 0 || extras->survivor_cap > 0xffffffffull))
             return RSC_ERR_INVALID_ARGUMENT;
+        if (extras->d_survivor_logprobs && !extras->d_survivor_ids) return RSC_ERR_INVALID_ARGUMENT;
         cp.out_nsurv = extras->d_n_survivors;
         cp.out_surv = extras->d_survivor_ids;
         cp.out_survp = extras->d_survivor_probs;
         cp.surv_cap = static_cast<uint32_t>(extras->survivor_cap);
     }
     DeviceGuard guard(s->device);
-    return sample_impl(s, d_logits, rows, vocab, row_stride, cp, d_out_ids, d_out_status,
-                       d_out_probs, static_cast<cudaStream_t>(stream));
+    cudaStream_t strm = static_cast<cudaStream_t>(stream);
+    if (!want_lp || rows == 0)
+        return sample_impl(s, d_logits, rows, vocab, row_stride, cp, d_out_ids, d_out_status,
+                           d_out_probs, strm);
+    // Log-probabilities: each row's log-sum-exp parts, from the streaming
+    // kernel's consumers when it streams the rows, else from one more pass.
+    if (!s->lse_parts &&
+        cudaMalloc(&s->lse_parts, s->max_rows * rsc::kStreamMaxSplits * sizeof(uint2)) != cudaSuccess)
+        return RSC_ERR_CUDA;
+    cudaError_t e = cudaMemsetAsync(s->lse_parts, 0, rows * rsc::kStreamMaxSplits * sizeof(uint2), strm);
+    if (e != cudaSuccess) return RSC_ERR_CUDA;
+    const bool fused = streams_rows(cp, vocab) && !(cp.topk_active && cp.top_k > rsc::kSmallTopK);
+    if (!fused) {
+        e = rsc::launch_lse_rows(d_logits, rows, static_cast<uint32_t>(vocab), row_stride, cp.scale,
+                                 s->lse_parts, rsc::kStreamMaxSplits, strm);
+        ++s->launches;
+        if (e != cudaSuccess) return RSC_ERR_CUDA;
+    } else {
+        cp.lse_parts = s->lse_parts;
+        cp.lse_stride = rsc::kStreamMaxSplits;
+    }
+    st = sample_impl(s, d_logits, rows, vocab, row_stride, cp, d_out_ids, d_out_status, d_out_probs,
+                     strm);
+    if (st != RSC_OK) return st;
+    e = rsc::launch_lse_finish(d_logits, rows, row_stride, cp.scale, s->lse_parts,
+                               rsc::kStreamMaxSplits, d_out_ids, d_out_status, extras->d_n_survivors,
+                               extras->d_survivor_ids, static_cast<uint32_t>(extras->survivor_cap),
+                               extras->d_row_logsumexp, extras->d_token_logprob,
+                               extras->d_survivor_logprobs, strm);
+    ++s->launches;
+    return cuda_status(e);
 }
 
 rsc_status rsc_sample_rows(rsc_sampler *s, const float *d_logits, size_t rows, size_t vocab,

@@ -215,7 +215,39 @@ struct CallParams {
     uint32_t surv_cap;
     float *out_survp = nullptr;   // nullable: rows x surv_cap survivor probabilities
     const rsc_params *row_params = nullptr;  // one parameter set per row (rsc_sample_rows)
+    // Log-sum-exp parts (nullable): for row r and part p of it, lse_parts[r *
+    // lse_stride + p] = (total_key of the part's largest scaled logit, sum of
+    // exp(v - that maximum) over the part), each part of the row one slot.
+    uint2 *lse_parts = nullptr;
+    uint32_t lse_stride = 0;
 };
+
+// Combines two (maximum, sum of exp(v - maximum)) partial log-sum-exps.
+__device__ __forceinline__ void lse_combine(float &m, float &s, float m2, float s2) {
+    if (m2 == kNegInf) return;
+    if (m == kNegInf) {
+        m = m2;
+        s = s2;
+        return;
+    }
+    if (m2 > m) {
+        s = s * __expf(m - m2) + s2;
+        m = m2;
+    } else {
+        s += s2 * __expf(m2 - m);
+    }
+}
+
+// Adds one scaled logit v to a partial log-sum-exp (m, s).
+__device__ __forceinline__ void lse_add(float &m, float &s, float v) {
+    if (v == kNegInf) return;
+    if (v > m) {
+        s = (m == kNegInf ? 0.0f : s * __expf(m - v)) + 1.0f;
+        m = v;
+    } else {
+        s += __expf(v - m);
+    }
+}
 
 // The parameters that apply to one row: the call's, or the row's own set,
 // derived field by field as the host derives the call's.

@@ -75,6 +75,19 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
 // with the other's work (cap: 64 registers a thread at 512 threads).
 constexpr uint32_t kLargeCtasPerSm = 2;
 
+// Log-probability outputs (lse.cu): lse_rows writes each row's partial
+// log-sum-exp into parts[row * stride] (for rows the streaming kernel's
+// consumers did not cover); lse_finish combines each row's `stride` parts and
+// writes the log-sum-exp, the chosen token's log-probability and the listed
+// survivors' log-probabilities (each output nullable).
+cudaError_t launch_lse_rows(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
+                            float scale, uint2 *parts, uint32_t stride, cudaStream_t stream);
+cudaError_t launch_lse_finish(const float *logits, size_t rows, size_t row_stride, float scale,
+                              const uint2 *parts, uint32_t stride, const uint32_t *ids,
+                              const int32_t *status, const uint32_t *n_surv, const uint32_t *surv,
+                              uint32_t cap, float *out_lse, float *out_logprob,
+                              float *out_surv_logp, cudaStream_t stream);
+
 cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, uint32_t *scratch, uint32_t slots, cudaStream_t stream);

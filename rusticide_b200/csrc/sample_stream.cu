@@ -91,6 +91,8 @@ struct StreamSmem {
     float tau_final[2];  // the consumers' last bound of the row (<= its k-th largest value)
     float warp_tau[2][kConsumerWarps];
     float st_max[2][kConsumerWarps];
+    float lse_m[2][kConsumerWarps];  // per consumer warp: partial log-sum-exp of the piece
+    float lse_s[2][kConsumerWarps];
     uint32_t chist[256];
     uint32_t csel[2];
     uint32_t error;
@@ -1047,7 +1049,9 @@ __device__ __noinline__ void epilogue_row(const CallParams &cp, const float *p, 
 
 // kRows: one parameter set per row (cp.row_params); a separate instance, so
 // that calls with one set for every row pay nothing for the lookups.
-template <bool kRecord, bool kRows = false>
+// kLse: the consumers also accumulate each row part's log-sum-exp of its
+// scaled logits (cp.lse_parts), for the log-probability outputs.
+template <bool kRecord, bool kRows = false, bool kLse = false>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab,
                    size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
@@ -1125,6 +1129,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             // NaN admits nothing (a row left to the epilogue).
             float tau = live ? -3.402823466e38f : __int_as_float(0x7fffffff);
             float lmax = kNegInf;  // this lane's largest scaled logit of the piece
+            float lse_m = kNegInf, lse_s = 0.0f;  // kLse: this lane's partial log-sum-exp
             // Scalar head and tail (at most 3 logits each).
             {
                 const uint32_t ntail = vocab - g.head - g.nbody;
@@ -1136,6 +1141,7 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 if (idx != ~0u) {
                     v = __fmul_rn(g.p[idx], scale);
                     lmax = fmaxf(lmax, v);
+                    if constexpr (kLse) lse_add(lse_m, lse_s, scale_logit(g.p[idx], scale));
                 }
                 append_candidate(L, count, ovf, v >= tau, total_key(v), idx + index_offset, kCap);
             }
@@ -1209,6 +1215,23 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 for (uint32_t jj = 1; jj < kPerThread; ++jj) cmr = fmaxf(cmr, m4[jj]);
                 const float cm = __fmul_rn(cmr, scale);
                 lmax = fmaxf(lmax, cm);
+                if constexpr (kLse) {
+                    // The slice's scaled maximum first, then its terms (NaN
+                    // reads as -inf, whose term is 0).
+                    if (cm > lse_m) {
+                        lse_s = lse_m == kNegInf ? 0.0f : lse_s * __expf(lse_m - cm);
+                        lse_m = cm;
+                    }
+                    if (lse_m != kNegInf) {
+#pragma unroll
+                        for (uint32_t jj = 0; jj < kPerThread; ++jj) {
+                            lse_s += __expf(scale_logit(f[jj].x, scale) - lse_m);
+                            lse_s += __expf(scale_logit(f[jj].y, scale) - lse_m);
+                            lse_s += __expf(scale_logit(f[jj].z, scale) - lse_m);
+                            lse_s += __expf(scale_logit(f[jj].w, scale) - lse_m);
+                        }
+                    }
+                }
                 if (cm >= tau) {
 #pragma unroll
                     for (uint32_t jj = 0; jj < kPerThread; ++jj) {
@@ -1278,6 +1301,18 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                 const float wm = warp_max(lmax);
                 if (lane == 0) sm.st_max[b][cw] = wm;
             }
+            if constexpr (kLse) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float m2 = __shfl_xor_sync(0xffffffffu, lse_m, o);
+                    const float s2 = __shfl_xor_sync(0xffffffffu, lse_s, o);
+                    lse_combine(lse_m, lse_s, m2, s2);
+                }
+                if (lane == 0) {
+                    sm.lse_m[b][cw] = lse_m;
+                    sm.lse_s[b][cw] = lse_s;
+                }
+            }
             if (threadIdx.x == 0) sm.tau_final[b] = tau;
             ConsumerSync::sync();  // the row's list is complete
             if (threadIdx.x == 0) mbar_arrive(&sm.list_full[b]);
@@ -1332,6 +1367,14 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
             if (__any_sync(0xffffffffu, !got)) {
                 if (lane == 0) atomicExch(&sm.error, 1u);
                 break;
+            }
+            if constexpr (kLse) {
+                if (lane == 0 && cp.lse_parts) {
+                    float m = kNegInf, sum = 0.0f;
+                    for (int w = 0; w < kConsumerWarps; ++w) lse_combine(m, sum, sm.lse_m[b][w], sm.lse_s[b][w]);
+                    cp.lse_parts[row * cp.lse_stride + pc.part] =
+                        make_uint2(total_key(m), __float_as_uint(sum));
+                }
             }
             uint32_t cnt = sm.count[b];
             const bool ov = sm.overflow[b] != 0 || cnt > kCap;
@@ -1843,7 +1886,9 @@ cudaError_t launch_stream_topk(const float *logits, size_t rows, uint32_t vocab,
     // The per-row instance also serves calls whose k is above the streaming
     // filter's: every row goes straight to the epilogue's two passes.
     const bool rows_instance = p.row_params || (p.topk_active && p.top_k > kSmallTopK);
-    auto kernel = rows_instance ? stream_topk_kernel<false, true> : stream_topk_kernel<false, false>;
+    auto kernel = rows_instance ? stream_topk_kernel<false, true>
+                  : p.lse_parts ? stream_topk_kernel<false, false, true>
+                                : stream_topk_kernel<false, false>;
     cudaError_t e = prepare(kernel, sizeof(StreamSmem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};

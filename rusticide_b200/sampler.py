@@ -223,24 +223,36 @@ class Engine:
 
     def sample_ex(self, logits: torch.Tensor, params: SamplingParams,
                   uniforms: Optional[torch.Tensor] = None,
-                  rng_states: Optional[torch.Tensor] = None, survivor_cap: int = 0):
+                  rng_states: Optional[torch.Tensor] = None, survivor_cap: int = 0,
+                  logprobs: bool = False):
         """rsc_sample_ex: rsc_sample plus each row's surviving candidate set and
         its probabilities. Returns (ids, status, probs, n_survivors,
-        survivor_ids[rows, cap], survivor_probs[rows, cap])."""
+        survivor_ids[rows, cap], survivor_probs[rows, cap]); with logprobs,
+        also (row_logsumexp, token_logprob, survivor_logprobs[rows, cap]):
+        log-probabilities over the whole row of scaled logits."""
         rows, vocab, stride = self._check_rows(logits)
         ids, status, probs = self._outputs(rows, True)
         nsurv = torch.empty(rows, dtype=torch.int32, device=self.device)
         cap = max(1, int(survivor_cap))
         surv = torch.full((rows, cap), -1, dtype=torch.int32, device=self.device)
         survp = torch.full((rows, cap), float("nan"), dtype=torch.float32, device=self.device)
+        lse = tok_lp = surv_lp = None
+        if logprobs:
+            lse = torch.full((rows,), float("nan"), dtype=torch.float32, device=self.device)
+            tok_lp = torch.full((rows,), float("nan"), dtype=torch.float32, device=self.device)
+            surv_lp = torch.full((rows, cap), float("nan"), dtype=torch.float32, device=self.device)
         ex = _lib.RscSampleExtras(nsurv.data_ptr(), surv.data_ptr() if survivor_cap else None,
                                   cap if survivor_cap else 0,
-                                  survp.data_ptr() if survivor_cap else None)
+                                  survp.data_ptr() if survivor_cap else None,
+                                  _ptr(lse), _ptr(tok_lp),
+                                  surv_lp.data_ptr() if (logprobs and survivor_cap) else None)
         c = params.to_c()
         check(self.lib.rsc_sample_ex(self._h, logits.data_ptr(), rows, vocab, stride,
                                      ctypes.byref(c), _ptr(uniforms), _ptr(rng_states),
                                      ids.data_ptr(), status.data_ptr(), _ptr(probs),
                                      ctypes.byref(ex), _stream_ptr(self.device)), "rsc_sample_ex")
+        if logprobs:
+            return ids, status, probs, nsurv, surv, survp, lse, tok_lp, surv_lp
         return ids, status, probs, nsurv, surv, survp
 
     def pick(self, logits: torch.Tensor, params: SamplingParams,

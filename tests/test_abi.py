@@ -45,7 +45,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_compute_free_calls():
     lib = _lib.load()
-    assert lib.rsc_abi_version() == 1
+    assert lib.rsc_abi_version() == 2
     assert lib.rsc_status_string(_lib.RSC_OK) == b"ok"
     assert lib.rsc_status_string(_lib.RSC_ERR_INVALID_SHAPE) == b"invalid shape"
     assert lib.rsc_shard_record_bytes(40) == 32 + 8 * (40 + _lib.RSC_SHARD_TIE_CAP)
