@@ -502,6 +502,80 @@ def vocab_sharded_leg(eng, world: int, rank: int, local: int, device, steps: int
     return res
 
 
+def emulated_shards(args) -> None:
+    """--config cfg4 --emulate-shards N on one GPU: the vocab-sharded step of
+    one rank at N GPUs, with the shards emulated on this GPU. Times one
+    rank's partial pass over its V/N columns (rsc_shard_partial), the merge of
+    N records (rsc_shard_merge) and the unsharded call on the same rows, and
+    checks the merged result bit for bit against the unsharded one. No
+    collective runs: the all-gather of the records is a concatenation here."""
+    import torch
+
+    from rusticide_b200 import SamplingParams, engine, synth
+
+    cfg = synth.CONFIGS["cfg4"]
+    n = args.emulate_shards
+    rows, vocab = (args.rows or cfg.rows), cfg.vocab
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    eng = engine(0)
+    params = SamplingParams(cfg.temperature, cfg.top_k, cfg.top_p)
+    x, u = device_logits(cfg, rows, 4242, device)
+    eng.ensure(rows, vocab)
+    bounds = [vocab * s // n for s in range(n + 1)]
+    rb = eng.shard_record_bytes(params.top_k)
+    gathered = torch.empty(n * rows * rb, dtype=torch.uint8, device=device)
+    recs = [gathered[s * rows * rb:(s + 1) * rows * rb] for s in range(n)]
+    outs = eng._outputs(rows, True)
+    base = eng._outputs(rows, True)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, k):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(k):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) * 1000.0 / k
+
+    def partials():
+        for s in range(n):
+            eng.shard_partial(x[:, bounds[s]:bounds[s + 1]], bounds[s], vocab, params, records=recs[s])
+
+    def merge():
+        eng.shard_merge(gathered, n, rows, vocab, params, uniforms=u, out=outs)
+
+    steps = max(args.steps, 1)
+    t_unsharded = timed(lambda: eng.sample(x, params, uniforms=u, out=base), steps)
+    t_one = timed(lambda: eng.shard_partial(x[:, bounds[0]:bounds[1]], bounds[0], vocab, params,
+                                            records=recs[0]), steps)
+    partials()
+    t_merge = timed(merge, steps)
+    merge()
+    torch.cuda.synchronize(device)
+    same = (torch.equal(outs[0], base[0]) and torch.equal(outs[1], base[1])
+            and torch.equal(outs[2].view(torch.int32), base[2].view(torch.int32)))
+    peak, _ = measured_peak()
+    width = bounds[1] - bounds[0]
+    emit({"metric": "vocab-sharded step of one rank, shards emulated on one GPU",
+          "config": {"workload": "cfg4", "rows": rows, "vocab": vocab, "n_shards": n,
+                     "shard_width": width, "temperature": cfg.temperature,
+                     "top_k": cfg.top_k, "top_p": cfg.top_p},
+          "steps": steps, "warmup": args.warmup,
+          "partial_us": t_one, "partial_gbs": rows * width * 4 / (t_one * 1e-6) / 1e9,
+          "partial_frac": rows * width * 4 / (t_one * 1e-6) / 1e9 / peak,
+          "merge_us": t_merge, "record_bytes_per_row": rb,
+          "rank_step_us_without_allgather": t_one + t_merge,
+          "unsharded_us": t_unsharded,
+          "strong_scaling_eff_without_allgather": t_unsharded / (n * (t_one + t_merge)),
+          "bit_exact_vs_unsharded": bool(same)})
+
+
 def lmhead_table(args) -> None:
     """Times the LM-head paths on one GPU (or tensor-parallel over the ranks):
     rsc_lmhead_sample (the GEMM with the sampler fused into its epilogue),
@@ -602,6 +676,9 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the parity, sustained and vocab-sharded legs (profiling captures)")
     ap.add_argument("--lmhead-rows", type=int, nargs="+", default=[1, 16, 64, 256, 1024])
+    ap.add_argument("--emulate-shards", type=int, default=0,
+                    help="--config cfg4 on one GPU: time one rank's partial pass and the merge "
+                         "of N shards emulated on this GPU")
     ap.add_argument("--fused-only", action="store_true",
                     help="--config lmhead: time only rsc_lmhead_sample (profiling captures)")
     args = ap.parse_args()
@@ -613,6 +690,11 @@ def main() -> None:
 
     if args.config == "lmhead":
         lmhead_table(args)
+        return
+    if args.emulate_shards > 0:
+        if args.config != "cfg4" or world != 1 or args.impl != "ours":
+            raise SystemExit("--emulate-shards runs --config cfg4 on one GPU (our arm)")
+        emulated_shards(args)
         return
 
     from rusticide_b200 import synth

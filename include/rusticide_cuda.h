@@ -377,6 +377,18 @@ RSC_API rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream
  * (for the benchmark's launch count). */
 RSC_API uint64_t rsc_launch_count(const rsc_sampler *sampler);
 
+/*
+ * Test hook of the bounded device waits (no counterpart in the reference,
+ * whose sampler never waits). Marks every scratch slot of the handle taken
+ * (hold != 0) or free (hold == 0), ordered on `stream`. While the slots are
+ * held, a row that the streaming kernel must finish with the large-row code
+ * (a candidate list overflowed by ties) waits for a slot for the library's
+ * wait limit (2 s of the GPU's global timer), gives up, and reports
+ * RSC_ROW_INTERNAL; every other row is sampled as usual and the device stays
+ * usable. Release the slots before sampling such rows again.
+ */
+RSC_API rsc_status rsc_debug_hold_scratch(rsc_sampler *sampler, int hold, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -248,4 +248,9 @@ unsafe extern "C" {
     ) -> c_int;
     pub(crate) fn rsc_expf(d_x: *const f32, d_y: *mut f32, n: usize, stream: *mut c_void) -> c_int;
     pub(crate) fn rsc_launch_count(sampler: *const RscSampler) -> u64;
+    pub(crate) fn rsc_debug_hold_scratch(
+        sampler: *mut RscSampler,
+        hold: c_int,
+        stream: *mut c_void,
+    ) -> c_int;
 }

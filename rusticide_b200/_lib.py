@@ -93,6 +93,7 @@ SIGNATURES = {
                                 _P, _P, _P]),
     "rsc_expf": (_ST, [_P, _P, _SZ, _P]),
     "rsc_launch_count": (ctypes.c_uint64, [_P]),
+    "rsc_debug_hold_scratch": (_ST, [_P, ctypes.c_int, _P]),
 }
 
 

@@ -139,8 +139,12 @@ rsc_status sample_impl(rsc_sampler *s, const float *logits, size_t rows, size_t 
     const bool small = streams_rows(cp, vocab);
     cudaError_t e;
     if (small) return stream_impl(s, logits, rows, v, row_stride, cp, ids, status, probs, stream);
-    e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
-                          s->large_slots, stream);
+    if (rsc::whole_takes(cp, vocab))
+        e = rsc::launch_whole(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
+                              s->large_slots, s->num_sms, stream);
+    else
+        e = rsc::launch_large(logits, rows, v, row_stride, cp, ids, status, probs, s->scratch,
+                              s->large_slots, stream);
     ++s->launches;
     return cuda_status(e);
 }
@@ -690,5 +694,13 @@ rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream) {
 }
 
 uint64_t rsc_launch_count(const rsc_sampler *s) { return s && s->alive ? s->launches : 0; }
+
+rsc_status rsc_debug_hold_scratch(rsc_sampler *s, int hold, void *stream) {
+    if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
+    DeviceGuard guard(s->device);
+    return cuda_status(cudaMemsetAsync(s->slot_lock, hold ? 0xff : 0,
+                                       s->large_slots * sizeof(uint32_t),
+                                       static_cast<cudaStream_t>(stream)));
+}
 
 }  // extern "C"

@@ -92,6 +92,19 @@ cudaError_t launch_large(const float *logits, size_t rows, uint32_t vocab, size_
                          const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                          float *out_probs, uint32_t *scratch, uint32_t slots, cudaStream_t stream);
 
+// Whole-row kernel (sample_whole.cu): one 1024-thread block per SM, a row at
+// a time, for rows with top-p on and top-k off at a normal scale whose
+// vocabulary is at most kWholeMaxToppVocab (their survivors are sorted in
+// shared memory). Scratch: `slots` regions of 4 * vocab uint32, one per
+// block. whole_takes says whether a call's rows go there (sample_logits, no
+// argmax, no survivor outputs, one parameter set for every row).
+constexpr uint32_t kWholeMaxToppVocab = 45056;
+bool whole_takes(const CallParams &p, size_t vocab);
+cudaError_t launch_whole(const float *logits, size_t rows, uint32_t vocab, size_t row_stride,
+                         const CallParams &p, uint32_t *out_ids, int32_t *out_status,
+                         float *out_probs, uint32_t *scratch, uint32_t slots, int num_sms,
+                         cudaStream_t stream);
+
 // LM-head GEMM with the sampler fused into its epilogue (lmhead.cu). A part's
 // record of a row holds at most kLmheadRowCap candidates, so top_k <=
 // kLmheadRowCap - RSC_SHARD_TIE_CAP; a row is spread over at most

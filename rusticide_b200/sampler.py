@@ -170,6 +170,14 @@ class Engine:
     def launch_count(self) -> int:
         return int(self.lib.rsc_launch_count(self._h))
 
+    def hold_scratch(self, hold: bool) -> None:
+        """rsc_debug_hold_scratch: marks the handle's scratch slots taken (or
+        free) on the current stream, so that a row needing one exercises the
+        bounded wait and reports RSC_ROW_INTERNAL. Test hook only."""
+        check(self.lib.rsc_debug_hold_scratch(self._h, 1 if hold else 0,
+                                               _stream_ptr(self.device)),
+              "rsc_debug_hold_scratch")
+
     # -- helpers --------------------------------------------------------------
     def _check_rows(self, logits: torch.Tensor) -> tuple[int, int, int]:
         if logits.device != self.device:

@@ -26,10 +26,77 @@ batch must give the tokens of the unsharded call bit for bit.
 
 from __future__ import annotations
 
+import time
 from typing import Optional, Tuple
 
 import torch
 import torch.distributed as dist
+
+
+class CollectiveError(RuntimeError):
+    """The records' all-gather failed: the backend reported an error (for
+    example a peer's connection closed when its process died). The process
+    group has been aborted, so no later collective on it can hang; the caller
+    rebuilds the group from the ranks still alive before sampling again."""
+
+
+class CollectiveTimeout(CollectiveError):
+    """The records' all-gather did not complete by its deadline: a rank left
+    or stopped calling the sampler while its process lives on. The group has
+    been aborted, as for CollectiveError."""
+
+
+def _abort_group(group: Optional[dist.ProcessGroup]) -> None:
+    """Ends every pending collective of `group` on this rank: the backend's
+    abort where it has one (NCCL: ncclCommAbort on its communicators), else
+    the group's destruction."""
+    pg = group if group is not None else dist.group.WORLD
+    try:
+        backend = pg._get_backend(torch.device("cuda")) if torch.cuda.is_available() else None
+    except Exception:
+        backend = None
+    if backend is not None and hasattr(backend, "abort"):
+        try:
+            backend.abort()
+            return
+        except Exception:
+            pass
+    try:
+        dist.destroy_process_group(group)
+    except Exception:
+        pass
+
+
+def gather_with_deadline(out: torch.Tensor, inp: torch.Tensor,
+                         group: Optional[dist.ProcessGroup], timeout_s: Optional[float],
+                         poll_s: float = 0.0005) -> None:
+    """all_gather_into_tensor(out, inp) that gives up after timeout_s seconds.
+
+    The collective is issued asynchronously and its completion polled from the
+    host (for NCCL, is_completed() reads the collective's CUDA event, the
+    counterpart of polling ncclCommGetAsyncError). Past the deadline the group
+    is aborted and CollectiveTimeout raised, so a rank that never joins cannot
+    hold the others forever. timeout_s None: a plain blocking all-gather
+    (bounded only by the process group's own timeout)."""
+    if timeout_s is None:
+        dist.all_gather_into_tensor(out, inp, group=group)
+        return
+    rank = dist.get_rank(group)
+    try:
+        work = dist.all_gather_into_tensor(out, inp, group=group, async_op=True)
+        deadline = time.monotonic() + timeout_s
+        while not work.is_completed():
+            if time.monotonic() > deadline:
+                _abort_group(group)
+                raise CollectiveTimeout(
+                    f"shard records all-gather not complete after {timeout_s:.3f} s (rank {rank})")
+            time.sleep(poll_s)
+        work.wait()
+    except CollectiveError:
+        raise
+    except RuntimeError as e:
+        _abort_group(group)
+        raise CollectiveError(f"shard records all-gather failed on rank {rank}: {e}") from e
 
 
 def vocab_shard(vocab: int, world: int, rank: int) -> Tuple[int, int]:
@@ -64,9 +131,13 @@ class VocabShardedSampler:
     (ids, status, probs) is the same on every rank.
     """
 
-    def __init__(self, engine, vocab: int, group: Optional[dist.ProcessGroup] = None):
+    def __init__(self, engine, vocab: int, group: Optional[dist.ProcessGroup] = None,
+                 timeout_s: Optional[float] = None):
+        """timeout_s: deadline of each records all-gather (None: wait as long
+        as the process group allows); see gather_with_deadline."""
         self.engine = engine
         self.group = group
+        self.timeout_s = timeout_s
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.vocab = int(vocab)
@@ -90,7 +161,7 @@ class VocabShardedSampler:
         rows = logits_shard.shape[0]
         records, gathered = self._buffers(rows, params.top_k, logits_shard.device)
         self.engine.shard_partial(logits_shard, self.offset, self.vocab, params, records=records)
-        dist.all_gather_into_tensor(gathered, records, group=self.group)
+        gather_with_deadline(gathered, records, self.group, self.timeout_s)
         return self.engine.shard_merge(gathered, self.world, rows, self.vocab, params,
                                        uniforms=uniforms, rng_states=rng_states,
                                        want_probs=want_probs, out=out)
@@ -111,7 +182,7 @@ class VocabShardedSampler:
         records, gathered = self._buffers(rows, params.top_k, hidden.device)
         self.engine.lmhead_partial(hidden, weight_shard, self.offset, self.vocab, params,
                                    records=records)
-        dist.all_gather_into_tensor(gathered, records, group=self.group)
+        gather_with_deadline(gathered, records, self.group, self.timeout_s)
         return self.engine.shard_merge(gathered, self.world, rows, self.vocab, params,
                                        uniforms=uniforms, rng_states=rng_states,
                                        want_probs=want_probs, out=out)

@@ -27,6 +27,7 @@ def test_header_declares_the_abi():
                  "rsc_greedy", "rsc_sample_with_temp", "rsc_pick", "rsc_pick_host",
                  "rsc_penalize", "rsc_rng_seed", "rsc_shard_partial", "rsc_shard_merge",
                  "rsc_shard_record_bytes", "rsc_expf", "rsc_launch_count", "rsc_status_string",
+                 "rsc_debug_hold_scratch",
                  "rsc_abi_version"]:
         assert must in names
 

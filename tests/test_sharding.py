@@ -20,7 +20,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from rusticide_b200 import SamplingParams, synth
-from rusticide_b200.sharding import VocabShardedSampler, row_shard, vocab_shard
+from rusticide_b200.sharding import (CollectiveError, CollectiveTimeout, VocabShardedSampler,
+                                     row_shard, vocab_shard)
 
 
 def test_vocab_shard_covers_the_vocabulary():
@@ -201,3 +202,67 @@ def test_sharded_lmhead_orchestration_matches_unsharded(world):
     want = [(int(t), int(st)) for t, st in zip(ref["token"], ref["status"])]
     for r in range(world):
         assert got[r] == want, f"rank {r}"
+
+
+def _rank_dropout_main(rank, world, port, rows, vocab, mode, q):
+    """Rank 0 samples with a short all-gather deadline. The other ranks leave
+    between steps without joining the collective: mode "stall" keeps their
+    process alive (a rank stuck elsewhere), mode "exit" ends it (a rank that
+    died)."""
+    import time as _t
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    if rank != 0:
+        q.put((rank, "left"))
+        if mode == "stall":
+            _t.sleep(5.0)
+        return  # no collective, no destroy: this rank is gone
+    x = synth.make_logits(rows, vocab, base_seed=77)
+    u = torch.from_numpy(synth.uniforms(rows, seed=5))
+    eng = _ColumnsEngine(max_width=vocab // world + vocab % world)
+    vs = VocabShardedSampler(eng, vocab, timeout_s=0.5)
+    mine = torch.from_numpy(np.ascontiguousarray(x[:, vs.offset:vs.offset + vs.width]))
+    t0 = _t.monotonic()
+    try:
+        vs.sample(mine, SamplingParams(0.8, 40, 0.95), uniforms=u)
+        q.put((0, ("no error", 0.0)))
+    except CollectiveTimeout:
+        q.put((0, ("timeout", _t.monotonic() - t0)))
+    except CollectiveError:
+        q.put((0, ("error", _t.monotonic() - t0)))
+
+
+@pytest.mark.parametrize("mode", ["stall", "exit"])
+def test_vocab_sharded_rank_dropout_is_detected(mode):
+    """Failure detection on the host: a rank that never joins the records'
+    all-gather makes the others raise instead of waiting for ever:
+    CollectiveTimeout after the deadline while its process lives, or
+    CollectiveError (or the timeout) once its connection has closed; the group
+    is aborted in both cases."""
+    world, rows, vocab = 2, 4, 501
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_dropout_main, args=(r, world, port, rows, vocab, mode, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        while len(got) < world:
+            rank, res = q.get(timeout=60)
+            got[rank] = res
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert got[1] == "left"
+    kind, secs = got[0]
+    if mode == "stall":
+        assert kind == "timeout", got[0]
+        assert 0.4 < secs < 20.0
+    else:
+        assert kind in ("timeout", "error"), got[0]
+        assert secs < 20.0
