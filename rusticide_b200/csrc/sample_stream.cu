@@ -726,6 +726,81 @@ __device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uin
     return min(count, kCap);
 }
 
+// merge_records for the vocab-sharded merge, with every part's entries in
+// flight at once: lane l serves part l / (32 / n) and reads every (32 / n)-th
+// of its entries, so a row costs one or two L2 round trips instead of one per
+// part. The union is the same set of entries (in another order, which the
+// finisher's ranks do not see), cut by the same bound and checked the same way.
+template <typename RecAt>
+__device__ uint32_t merge_parts_batched(CandList &L, FinishWork &fw, RecAt rec_at, uint32_t n,
+                                        uint32_t cap_entries, const CallParams &cp, bool *ok) {
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t flags = 0, ndrop = 0, ncand = 0;
+    float tau_s = -3.402823466e38f;
+    if (lane < n) {
+        const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(lane));
+        ncand = min(__ldcg(h + 3), cap_entries);
+        ndrop = __ldcg(h + 4);
+        flags = __ldcg(h + 6);
+        tau_s = __uint_as_float(__ldcg(h + 7));
+    }
+    bool good = !__any_sync(0xffffffffu, flags != 0u);
+    float tau = tau_s;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tau = fmaxf(tau, __shfl_xor_sync(0xffffffffu, tau, o));
+    const bool any_dropped = __any_sync(0xffffffffu, ndrop > 0u);
+    const uint32_t lps = 32u / n;  // lanes per part (n <= 32)
+    const uint32_t part = lane / lps, sub = lane % lps;
+    const uint32_t nc = __shfl_sync(0xffffffffu, ncand, part < n ? part : 0u);
+    const bool mine = part < n;
+    const uint32_t *rkey =
+        mine ? reinterpret_cast<const uint32_t *>(rec_at(part)) + 8 : nullptr;
+    const uint32_t *ridx = mine ? rkey + cap_entries : nullptr;
+    const uint32_t most = (cap_entries + lps - 1) / lps;  // entries a lane may hold
+    const uint32_t below = (1u << lane) - 1u;
+    uint32_t count = 0;
+    constexpr uint32_t kBatchLoads = 8;
+    for (uint32_t q0 = 0; q0 < most && good; q0 += kBatchLoads) {
+        uint32_t kk[kBatchLoads], ii[kBatchLoads];
+#pragma unroll
+        for (uint32_t q = 0; q < kBatchLoads; ++q) {
+            const uint32_t j = sub + (q0 + q) * lps;
+            const bool in = mine && j < nc;
+            kk[q] = in ? __ldcg(rkey + j) : 0u;
+            ii[q] = in ? __ldcg(ridx + j) : 0u;
+        }
+#pragma unroll
+        for (uint32_t q = 0; q < kBatchLoads; ++q) {
+            const uint32_t j = sub + (q0 + q) * lps;
+            const bool keep = mine && j < nc && key_to_float(kk[q]) >= tau;
+            const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+            const uint32_t pos = count + __popc(ballot & below);
+            if (keep && pos < kCap) {
+                L.key[pos] = kk[q];
+                L.idx[pos] = ii[q];
+            }
+            count += __popc(ballot);
+        }
+    }
+    if (count > kCap) good = false;
+    __syncwarp();
+    if (good && any_dropped) {
+        uint32_t floor_key = 0u;
+        const bool have_kth = cp.topk_active && count >= cp.top_k;
+        if (have_kth) {
+            const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
+                count, cp.top_k, [&](uint32_t i) { return L.key[i]; }, fw.hist, fw.sel);
+            floor_key = kth == kKeyPosZero ? kKeyNegZero : kth;
+        }
+        for (uint32_t s = 0; s < n; ++s) {
+            const uint32_t *h = reinterpret_cast<const uint32_t *>(rec_at(s));
+            if (__ldcg(h + 4) > 0 && (!have_kth || __ldcg(h + 5) >= floor_key)) good = false;
+        }
+    }
+    *ok = good;
+    return min(count, kCap);
+}
+
 // --- work schedule -------------------------------------------------------------
 //
 // The batch is rows x nch chunks (nch = ceil(vocab / kChunk), the same for
@@ -1586,7 +1661,7 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
     for (size_t row = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; row < rows;
          row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
         bool ok = true;
-        const uint32_t count = merge_records(
+        const uint32_t count = merge_parts_batched(
             L, fw, [&](uint32_t part) { return records + (part * rows + row) * rec_bytes; },
             static_cast<uint32_t>(n_shards), cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
         if (!ok) {
