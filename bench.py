@@ -468,12 +468,23 @@ def vocab_sharded_leg(eng, world: int, rank: int, local: int, device, steps: int
         t = timed(lambda: vs.sample(view, params, uniforms=u, out=outs), steps)
         vs.sample(view, params, uniforms=u, out=outs)
         torch.cuda.synchronize(device)
+        # The step's three parts timed apart (same buffers, every rank).
+        records, gathered = vs._buffers(rows, params.top_k, device)
+        t_part = timed(lambda: eng.shard_partial(view, vs.offset, vocab, params, records=records),
+                       steps)
+        t_gather = timed(lambda: dist.all_gather_into_tensor(gathered, records), steps)
+        t_merge = timed(lambda: eng.shard_merge(gathered, world, rows, vocab, params, uniforms=u,
+                                                out=outs), steps)
+        vs.sample(view, params, uniforms=u, out=outs)
+        torch.cuda.synchronize(device)
         same = (torch.equal(outs[0], base[0]) and torch.equal(outs[1], base[1])
                 and torch.equal(outs[2].view(torch.int32), base[2].view(torch.int32)))
-        stat = torch.tensor([t, 0.0 if same else 1.0, float(vs.width)], dtype=torch.float64,
-                            device=device)
+        stat = torch.tensor([t, 0.0 if same else 1.0, float(vs.width), t_part, t_gather, t_merge],
+                            dtype=torch.float64, device=device)
         dist.all_reduce(stat, op=dist.ReduceOp.MAX)
         t_max, any_diff, wmax = float(stat[0]), float(stat[1]), float(stat[2])
+        parts = {"partial_us": float(stat[3]), "allgather_us": float(stat[4]),
+                 "merge_us": float(stat[5])}
         per_gpu_bytes = rows * wmax * 4
         res.update({
             "us_per_step": t_max,
@@ -482,6 +493,7 @@ def vocab_sharded_leg(eng, world: int, rank: int, local: int, device, steps: int
             "per_gpu_frac": per_gpu_bytes / (t_max * 1e-6) / 1e9 / peak,
             "strong_scaling_eff": t_unsharded / (world * t_max),
             "bit_exact_vs_unsharded": any_diff == 0.0,
+            "parts_max_over_ranks": parts,
             "note": "us_per_step = partial + NCCL all-gather + merge, max over ranks; "
                     "strong_scaling_eff = unsharded 1-GPU time / (N x sharded time)",
         })

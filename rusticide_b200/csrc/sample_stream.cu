@@ -1126,10 +1126,16 @@ __device__ __noinline__ void epilogue_row(const CallParams &cp, const float *p, 
 // that calls with one set for every row pay nothing for the lookups.
 // kLse: the consumers also accumulate each row part's log-sum-exp of its
 // scaled logits (cp.lse_parts), for the log-probability outputs.
+// cp is a grid constant: the out-of-line epilogue functions take it by
+// reference, and the address of a grid constant points into the parameter
+// space, where a plain parameter would be copied to every thread's stack (96
+// bytes of local-memory stores per thread and launch, 13.5 MB per 512-row
+// call, most of the kernel's DRAM writes).
 template <bool kRecord, bool kRows = false, bool kLse = false>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab,
-                   size_t row_stride, CallParams cp, uint32_t *__restrict__ out_ids,
+                   size_t row_stride, const __grid_constant__ CallParams cp,
+                   uint32_t *__restrict__ out_ids,
                    int32_t *__restrict__ out_status, float *__restrict__ out_probs,
                    uint32_t *__restrict__ scratch, uint32_t slots, uint32_t *__restrict__ slot_lock,
                    uint32_t index_offset, unsigned char *__restrict__ records, size_t rec_bytes,
@@ -1639,7 +1645,9 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
 
 // Vocab-sharded merge: each warp gathers the shards' records of one row into
 // its candidate list and finishes the row exactly as the streaming kernel does.
-constexpr int kMergeWarps = 4;
+// Two warps per CTA: 31 KB of shared memory a CTA, so 7 CTAs (14 warps) share
+// an SM, against 12 warps with four-warp CTAs.
+constexpr int kMergeWarps = 2;
 
 struct MergeSmem {
     CandList list[kMergeWarps];
