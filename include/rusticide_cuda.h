@@ -373,6 +373,41 @@ RSC_API rsc_status rsc_lmhead_partial(rsc_sampler *sampler, const void *d_hidden
  */
 RSC_API rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream);
 
+/*
+ * Vocab-sharded sampling over peer memory (no reference counterpart: the
+ * reference samples a whole row on one CPU thread). The same result as
+ * rsc_shard_partial + an all-gather + rsc_shard_merge, with the all-gather
+ * replaced by reads of the other ranks' record arrays in place, over NVLink.
+ * Each rank keeps its record array and an array of n_shards ready words in
+ * memory that every rank can address (for example a symmetric allocation),
+ * and per step:
+ *   1. rsc_shard_partial into its own record array;
+ *   2. rsc_shard_publish(d_ready_ptrs, n_shards, my_shard, step): after the
+ *      stream's earlier work, stores `step` into word my_shard of every rank's
+ *      ready array (d_ready_ptrs: a device array of the n_shards ranks' ready
+ *      arrays), with a system-wide fence first;
+ *   3. rsc_shard_merge_peers(..., d_peer_records, d_ready, step, ...):
+ *      d_peer_records is a device array of the n_shards ranks' record arrays
+ *      (rank order), d_ready this rank's ready array. The kernel waits until
+ *      every rank's word has reached `step` (wrap-around compare), bounded by
+ *      the library's 2 s wait limit (rows then report RSC_ROW_INTERNAL), and
+ *      merges as rsc_shard_merge.
+ * `step` must increase by one per call. A rank rewrites its record array only
+ * in its next step's partial pass, which follows its own merge of this step,
+ * and every rank's merge of the next step waits for that rank's next
+ * publication; two record arrays used alternately (by step parity) therefore
+ * keep a slow rank's reads of this step intact. n_shards <= 32 and
+ * n_shards * (top_k + RSC_SHARD_TIE_CAP) <= 512, else RSC_ERR_CAPACITY.
+ */
+RSC_API rsc_status rsc_shard_merge_peers(rsc_sampler *sampler, const void *const *d_peer_records,
+                                         const uint32_t *d_ready, uint32_t step, size_t n_shards,
+                                         size_t rows, size_t global_vocab,
+                                         const rsc_params *params, const float *d_uniforms,
+                                         uint64_t *d_rng_states, uint32_t *d_out_ids,
+                                         int32_t *d_out_status, float *d_out_probs, void *stream);
+RSC_API rsc_status rsc_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards,
+                                     size_t my_shard, uint32_t step, void *stream);
+
 /* Number of kernel launches the library issued since the handle was created
  * (for the benchmark's launch count). */
 RSC_API uint64_t rsc_launch_count(const rsc_sampler *sampler);

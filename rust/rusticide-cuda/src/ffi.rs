@@ -247,6 +247,29 @@ unsafe extern "C" {
         stream: *mut c_void,
     ) -> c_int;
     pub(crate) fn rsc_expf(d_x: *const f32, d_y: *mut f32, n: usize, stream: *mut c_void) -> c_int;
+    pub(crate) fn rsc_shard_merge_peers(
+        sampler: *mut RscSampler,
+        d_peer_records: *const *const c_void,
+        d_ready: *const u32,
+        step: u32,
+        n_shards: usize,
+        rows: usize,
+        global_vocab: usize,
+        params: *const RscParams,
+        d_uniforms: *const f32,
+        d_rng_states: *mut u64,
+        d_out_ids: *mut u32,
+        d_out_status: *mut i32,
+        d_out_probs: *mut f32,
+        stream: *mut c_void,
+    ) -> c_int;
+    pub(crate) fn rsc_shard_publish(
+        d_ready_ptrs: *const *mut u32,
+        n_shards: usize,
+        my_shard: usize,
+        step: u32,
+        stream: *mut c_void,
+    ) -> c_int;
     pub(crate) fn rsc_launch_count(sampler: *const RscSampler) -> u64;
     pub(crate) fn rsc_debug_hold_scratch(
         sampler: *mut RscSampler,

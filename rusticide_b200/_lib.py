@@ -84,6 +84,9 @@ SIGNATURES = {
     "rsc_shard_record_bytes": (_SZ, [ctypes.c_uint32]),
     "rsc_shard_partial": (_ST, [_P, _P, _SZ, _SZ, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P]),
     "rsc_shard_merge": (_ST, [_P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P, _P]),
+    "rsc_shard_merge_peers": (_ST, [_P, _P, _P, ctypes.c_uint32, _SZ, _SZ, _SZ,
+                                    ctypes.POINTER(RscParams), _P, _P, _P, _P, _P, _P]),
+    "rsc_shard_publish": (_ST, [_P, _SZ, _SZ, ctypes.c_uint32, _P]),
     "rsc_sample_noalloc": (_ST, [_P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P,
                                  _P]),
     "rsc_lmhead_logits": (_ST, [_P, _P, _P, _SZ, _SZ, _SZ, _P, _P]),

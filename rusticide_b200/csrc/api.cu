@@ -693,6 +693,42 @@ rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream) {
     return cuda_status(rsc::launch_expf(d_x, d_y, n, static_cast<cudaStream_t>(stream)));
 }
 
+rsc_status rsc_shard_merge_peers(rsc_sampler *s, const void *const *d_peer_records,
+                                 const uint32_t *d_ready, uint32_t step, size_t n_shards,
+                                 size_t rows, size_t global_vocab, const rsc_params *params,
+                                 const float *d_uniforms, uint64_t *d_rng_states,
+                                 uint32_t *d_out_ids, int32_t *d_out_status, float *d_out_probs,
+                                 void *stream) {
+    if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
+    if (!params || n_shards == 0) return RSC_ERR_INVALID_ARGUMENT;
+    if (global_vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
+    if (rows > s->max_rows) return RSC_ERR_CAPACITY;
+    if (rows > 0 && (!d_peer_records || !d_ready || !d_out_ids || !d_out_status))
+        return RSC_ERR_INVALID_ARGUMENT;
+    rsc::CallParams cp = make_params(*params, global_vocab, d_uniforms, d_rng_states);
+    if (!cp.topk_active || !cp.normal_scale) return RSC_ERR_INVALID_ARGUMENT;
+    // One warp merges a row: the ranks' records must fit its candidate list.
+    const size_t cap = static_cast<size_t>(params->top_k) + RSC_SHARD_TIE_CAP;
+    if (n_shards > 32 || n_shards * cap > rsc::kSmallCap) return RSC_ERR_CAPACITY;
+    if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows == 0) return RSC_OK;
+    DeviceGuard guard(s->device);
+    cudaError_t e = rsc::launch_shard_merge_peers(
+        d_peer_records, d_ready, step, n_shards, rows, rsc::shard_record_bytes(params->top_k), cp,
+        d_out_ids, d_out_status, d_out_probs, static_cast<cudaStream_t>(stream));
+    ++s->launches;
+    return cuda_status(e);
+}
+
+rsc_status rsc_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards, size_t my_shard,
+                             uint32_t step, void *stream) {
+    if (!d_ready_ptrs || n_shards == 0 || n_shards > 1024 || my_shard >= n_shards)
+        return RSC_ERR_INVALID_ARGUMENT;
+    return cuda_status(rsc::launch_shard_publish(d_ready_ptrs, n_shards,
+                                                 static_cast<uint32_t>(my_shard), step,
+                                                 static_cast<cudaStream_t>(stream)));
+}
+
 uint64_t rsc_launch_count(const rsc_sampler *s) { return s && s->alive ? s->launches : 0; }
 
 rsc_status rsc_debug_hold_scratch(rsc_sampler *s, int hold, void *stream) {

@@ -151,6 +151,18 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
                                  void *records, size_t rec_bytes, int num_sms,
                                  cudaStream_t stream);
 
+// The merge reading each rank's records in place (peer memory): d_peer_records
+// is a device array of n_shards record-array pointers (n_shards <= 32; one warp
+// merges a row, so n_shards * (k + RSC_SHARD_TIE_CAP) <= kSmallCap), d_ready
+// n_shards words of this GPU that rank p sets to the step it has published.
+cudaError_t launch_shard_merge_peers(const void *const *d_peer_records, const uint32_t *d_ready,
+                                     uint32_t step, size_t n_shards, size_t rows,
+                                     size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
+                                     int32_t *out_status, float *out_probs, cudaStream_t stream);
+// Stores `step` into word my_shard of every rank's ready array (d_ready_ptrs: a
+// device array of n_shards pointers, peer memory) after a system-wide fence.
+cudaError_t launch_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards, uint32_t my_shard,
+                                 uint32_t step, cudaStream_t stream);
 cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows, size_t rec_bytes,
                                const CallParams &p, uint32_t *out_ids, int32_t *out_status,
                                float *out_probs, int num_sms, cudaStream_t stream);

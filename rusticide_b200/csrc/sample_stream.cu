@@ -1648,6 +1648,8 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
 // Two warps per CTA: 31 KB of shared memory a CTA, so 7 CTAs (14 warps) share
 // an SM, against 12 warps with four-warp CTAs.
 constexpr int kMergeWarps = 2;
+// Most ranks the peer-memory merge reads (records in flight per warp).
+constexpr uint32_t kMergeMaxPeers = 32;
 
 struct MergeSmem {
     CandList list[kMergeWarps];
@@ -1682,6 +1684,81 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
             continue;
         }
         finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+    }
+}
+
+// The vocab-sharded merge reading every rank's records in place over NVLink
+// (peer memory), instead of from an all-gathered copy: records[p] is rank p's
+// record array ([rows] records, in rank p's memory, mapped here), ready[p] a
+// word in this GPU's memory that rank p sets to the step it has published.
+// Before reading, each CTA waits (bounded) until every ready[p] has reached
+// `step`; a wait that runs out marks the CTA's rows RSC_ROW_INTERNAL and reads
+// nothing. The rows then merge exactly as in shard_merge_kernel.
+__global__ void __launch_bounds__(kMergeWarps * 32)
+shard_merge_peers_kernel(const unsigned char *const *__restrict__ records,
+                         const uint32_t *ready, uint32_t step, uint32_t n_shards, size_t rows,
+                         size_t rec_bytes, const __grid_constant__ CallParams cp,
+                         uint32_t *__restrict__ out_ids, int32_t *__restrict__ out_status,
+                         float *__restrict__ out_probs) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    MergeSmem &sm = *reinterpret_cast<MergeSmem *>(smem_raw);
+    __shared__ uint32_t all_ready;
+    __shared__ const unsigned char *base[kMergeMaxPeers];
+    load_exp_table(sm.exp_tab);
+    if (threadIdx.x < n_shards) base[threadIdx.x] = records[threadIdx.x];
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        const unsigned long long t0 = global_ns();
+        for (uint32_t p = 0; p < n_shards && ok; ++p) {
+            while (true) {
+                uint32_t v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ready + p) : "memory");
+                if (static_cast<int32_t>(v - step) >= 0) break;
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(200);
+            }
+        }
+        all_ready = ok ? 1u : 0u;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    CandList &L = sm.list[warp];
+    FinishWork &fw = sm.fw[warp];
+    for (size_t row = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; row < rows;
+         row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
+        bool ok = all_ready != 0u;
+        uint32_t count = 0;
+        if (ok)
+            count = merge_parts_batched(
+                L, fw, [&](uint32_t part) { return base[part] + row * rec_bytes; }, n_shards,
+                cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
+        if (!ok) {
+            if (lane == 0) {
+                out_ids[row] = 0;
+                out_status[row] = RSC_ROW_INTERNAL;
+                if (out_probs) out_probs[row] = __uint_as_float(0x7fc00000u);
+            }
+            __syncwarp();
+            continue;
+        }
+        finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+    }
+}
+
+// Publishes this rank's records of `step` to every rank: after the stream's
+// earlier work (the partial pass) has completed, a system-wide fence makes
+// its record writes visible, then thread p stores `step` into rank p's ready
+// word for this rank (ready_ptrs[p] + my_shard, peer memory).
+__global__ void shard_publish_kernel(uint32_t *const *__restrict__ ready_ptrs, uint32_t n_shards,
+                                     uint32_t my_shard, uint32_t step) {
+    __threadfence_system();
+    const uint32_t p = threadIdx.x;
+    if (p < n_shards) {
+        uint32_t *dst = ready_ptrs[p] + my_shard;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst), "r"(step) : "memory");
     }
 }
 
@@ -2057,6 +2134,32 @@ cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows
     shard_merge_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem), stream>>>(
         static_cast<const unsigned char *>(records), n_shards, rows, rec_bytes, p, out_ids,
         out_status, out_probs);
+    return cudaGetLastError();
+}
+
+
+cudaError_t launch_shard_merge_peers(const void *const *d_peer_records, const uint32_t *d_ready,
+                                     uint32_t step, size_t n_shards, size_t rows,
+                                     size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
+                                     int32_t *out_status, float *out_probs,
+                                     cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    if (n_shards == 0 || n_shards > kMergeMaxPeers) return cudaErrorInvalidValue;
+    cudaError_t e = prepare(shard_merge_peers_kernel, sizeof(MergeSmem));
+    if (e != cudaSuccess) return e;
+    const size_t grid = (rows + kMergeWarps - 1) / kMergeWarps;
+    shard_merge_peers_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem),
+                               stream>>>(
+        reinterpret_cast<const unsigned char *const *>(d_peer_records), d_ready, step,
+        static_cast<uint32_t>(n_shards), rows, rec_bytes, p, out_ids, out_status, out_probs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards, uint32_t my_shard,
+                                 uint32_t step, cudaStream_t stream) {
+    if (n_shards == 0 || n_shards > 1024 || my_shard >= n_shards) return cudaErrorInvalidValue;
+    shard_publish_kernel<<<1, 32 * static_cast<unsigned>((n_shards + 31) / 32), 0, stream>>>(
+        d_ready_ptrs, static_cast<uint32_t>(n_shards), my_shard, step);
     return cudaGetLastError();
 }
 

@@ -347,6 +347,32 @@ class Engine:
               "rsc_shard_partial")
         return records
 
+    def shard_publish(self, ready_ptrs: torch.Tensor, n_shards: int, my_shard: int, step: int) -> None:
+        """rsc_shard_publish: `step` into word my_shard of every rank's ready
+        array (ready_ptrs: int64 device tensor of the ranks' ready arrays)."""
+        check(self.lib.rsc_shard_publish(ready_ptrs.data_ptr(), int(n_shards), int(my_shard),
+                                         int(step) & 0xFFFFFFFF, _stream_ptr(self.device)),
+              "rsc_shard_publish")
+
+    def shard_merge_peers(self, peer_records: torch.Tensor, ready: int, step: int, n_shards: int,
+                          rows: int, global_vocab: int, params: SamplingParams,
+                          uniforms: Optional[torch.Tensor] = None,
+                          rng_states: Optional[torch.Tensor] = None, want_probs: bool = True,
+                          out=None):
+        """rsc_shard_merge_peers: the merge reading every rank's record array
+        in place (peer_records: int64 device tensor of the ranks' record-array
+        addresses; ready: address of this rank's ready words)."""
+        self.ensure(rows, 1)
+        ids, status, probs = out if out is not None else self._outputs(rows, want_probs)
+        c = params.to_c()
+        check(self.lib.rsc_shard_merge_peers(self._h, peer_records.data_ptr(), int(ready),
+                                             int(step) & 0xFFFFFFFF, int(n_shards), rows,
+                                             int(global_vocab), ctypes.byref(c), _ptr(uniforms),
+                                             _ptr(rng_states), ids.data_ptr(), status.data_ptr(),
+                                             _ptr(probs), _stream_ptr(self.device)),
+              "rsc_shard_merge_peers")
+        return ids, status, probs
+
     def shard_merge(self, gathered: torch.Tensor, n_shards: int, rows: int, global_vocab: int,
                     params: SamplingParams, uniforms: Optional[torch.Tensor] = None,
                     rng_states: Optional[torch.Tensor] = None, want_probs: bool = True, out=None):

@@ -186,3 +186,66 @@ class VocabShardedSampler:
         return self.engine.shard_merge(gathered, self.world, rows, self.vocab, params,
                                        uniforms=uniforms, rng_states=rng_states,
                                        want_probs=want_probs, out=out)
+
+
+class PeerVocabShardedSampler(VocabShardedSampler):
+    """The vocab-sharded step with the all-gather replaced by reads in place:
+    each rank's records and ready words live in a symmetric allocation (every
+    rank maps every other rank's copy), the partial pass writes this rank's
+    records, rsc_shard_publish tells every rank the step is ready, and
+    rsc_shard_merge_peers reads all ranks' records over NVLink (plain loads)
+    once each rank's ready word for this step has arrived. Two record arrays,
+    used by step parity, keep a slow rank's reads intact (see the C header).
+    The result equals VocabShardedSampler's and the unsharded call's. Needs
+    one warp merge per row: world * (k + 24) <= 512 entries and world <= 32."""
+
+    READY_BYTES = 256  # ready words of up to 64 ranks
+
+    def __init__(self, engine, vocab: int, group: Optional[dist.ProcessGroup] = None):
+        super().__init__(engine, vocab, group)
+        self._peer = None
+        self._step = 0
+
+    def _peer_state(self, rows: int, top_k: int, device):
+        key = (rows, top_k, str(device))
+        if self._peer is None or self._peer["key"] != key:
+            import os
+            # Plain peer loads only: no multicast object is needed.
+            os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+            import torch.distributed._symmetric_memory as symm
+            rb = self.engine.shard_record_bytes(top_k)
+            span = (rows * rb + 255) // 256 * 256
+            buf = symm.empty(self.READY_BYTES + 2 * span, dtype=torch.uint8, device=device)
+            buf.zero_()
+            torch.cuda.synchronize(device)
+            handle = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+            ptrs = [int(p) for p in handle.buffer_ptrs]
+            if len(ptrs) != self.world:
+                raise RuntimeError(f"symmetric allocation spans {len(ptrs)} ranks, not {self.world}")
+            recs = [torch.tensor([p + self.READY_BYTES + par * span for p in ptrs],
+                                 dtype=torch.int64, device=device) for par in (0, 1)]
+            ready_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+            # Every rank has zeroed its ready words before any rank publishes.
+            dist.barrier(group=self.group)
+            self._peer = {"key": key, "buf": buf, "handle": handle, "recs": recs,
+                          "ready_ptrs": ready_ptrs, "rb": rb, "span": span}
+            self._step = 0
+        return self._peer
+
+    def sample(self, logits_shard: torch.Tensor, params, uniforms: Optional[torch.Tensor] = None,
+               rng_states: Optional[torch.Tensor] = None, want_probs: bool = True, out=None):
+        if logits_shard.dim() != 2 or logits_shard.shape[1] != self.width:
+            raise ValueError(f"rank {self.rank} expects [rows, {self.width}] logits, "
+                             f"got {tuple(logits_shard.shape)}")
+        rows = logits_shard.shape[0]
+        st = self._peer_state(rows, params.top_k, logits_shard.device)
+        self._step += 1
+        step, par = self._step, self._step & 1
+        off = self.READY_BYTES + par * st["span"]
+        mine = st["buf"][off:off + rows * st["rb"]]
+        self.engine.shard_partial(logits_shard, self.offset, self.vocab, params, records=mine)
+        self.engine.shard_publish(st["ready_ptrs"], self.world, self.rank, step)
+        return self.engine.shard_merge_peers(st["recs"][par], st["buf"].data_ptr(), step,
+                                             self.world, rows, self.vocab, params,
+                                             uniforms=uniforms, rng_states=rng_states,
+                                             want_probs=want_probs, out=out)

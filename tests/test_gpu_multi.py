@@ -172,3 +172,61 @@ def test_vocab_sharded_nccl_matches_unsharded():
         assert got[r] == want, f"rank {r}"
     ref = O.sample_rows(x, O.params(0.8, 40, 0.95), u, threads=4)
     assert want[0] == [int(t) for t in ref["token"]]
+
+
+PEER_ROWS, PEER_VOCAB, PEER_STEPS = 512, 151936, 3
+
+
+def _peer_inputs(step):
+    g = torch.Generator().manual_seed(500 + step)
+    x = torch.randn(PEER_ROWS, PEER_VOCAB, generator=g) * 2.0
+    u = torch.rand(PEER_ROWS, generator=g)
+    return x, u
+
+
+def _rank_peer(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    from rusticide_b200 import engine
+    from rusticide_b200.sharding import PeerVocabShardedSampler
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    vs = None
+    try:
+        vs = PeerVocabShardedSampler(engine(rank), PEER_VOCAB)
+        res = []
+        for step in range(PEER_STEPS):
+            x, u = _peer_inputs(step)
+            mine = x[:, vs.offset:vs.offset + vs.width].contiguous().to(dev)
+            ids, status, probs = vs.sample(mine, SamplingParams(0.8, 40, 0.95), uniforms=u.to(dev))
+            res.append((ids.cpu().numpy().tolist(), status.cpu().numpy().tolist(),
+                        probs.cpu().numpy().view(np.uint32).tolist()))
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        q.put((rank, res, None, None))
+    finally:
+        del vs
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_memory_vocab_sharded_matches_unsharded():
+    """The records read in place over NVLink (no all-gather): three steps in a
+    row (both record arrays, the step counter), every rank bit for bit equal to
+    the unsharded call on the whole rows."""
+    from rusticide_b200 import engine
+    world = min(torch.cuda.device_count(), 4)
+    got = _run_ranks(_rank_peer, world)
+    dev = torch.device("cuda", 0)
+    for step in range(PEER_STEPS):
+        x, u = _peer_inputs(step)
+        ids, st, pb = engine(0).sample(x.to(dev), SamplingParams(0.8, 40, 0.95), uniforms=u.to(dev))
+        want = (ids.cpu().numpy().tolist(), st.cpu().numpy().tolist(),
+                pb.cpu().numpy().view(np.uint32).tolist())
+        for r in range(world):
+            assert got[r][0][step] == want, f"rank {r} step {step}"
