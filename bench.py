@@ -497,6 +497,26 @@ def vocab_sharded_leg(eng, world: int, rank: int, local: int, device, steps: int
             "note": "us_per_step = partial + NCCL all-gather + merge, max over ranks; "
                     "strong_scaling_eff = unsharded 1-GPU time / (N x sharded time)",
         })
+        # The same step with the records read in place over NVLink (peer
+        # memory) instead of all-gathered by NCCL.
+        from rusticide_b200.sharding import PeerVocabShardedSampler
+        pvs = PeerVocabShardedSampler(eng, vocab)
+        pouts = eng._outputs(rows, True)
+        t_peer = timed(lambda: pvs.sample(view, params, uniforms=u, out=pouts), steps)
+        pvs.sample(view, params, uniforms=u, out=pouts)
+        torch.cuda.synchronize(device)
+        psame = (torch.equal(pouts[0], base[0]) and torch.equal(pouts[1], base[1])
+                 and torch.equal(pouts[2].view(torch.int32), base[2].view(torch.int32)))
+        pstat = torch.tensor([t_peer, 0.0 if psame else 1.0], dtype=torch.float64, device=device)
+        dist.all_reduce(pstat, op=dist.ReduceOp.MAX)
+        dist.barrier(device_ids=[local])
+        res["peer_exchange"] = {
+            "us_per_step": float(pstat[0]),
+            "strong_scaling_eff": t_unsharded / (world * float(pstat[0])),
+            "bit_exact_vs_unsharded": float(pstat[1]) == 0.0,
+            "note": "partial + publish + merge reading every rank's records over NVLink "
+                    "(rsc_shard_merge_peers), max over ranks"}
+        del pvs
         got = outs
     else:
         res["us_per_step"] = t_unsharded
