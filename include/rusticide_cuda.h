@@ -377,36 +377,57 @@ RSC_API rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream
  * Vocab-sharded sampling over peer memory (no reference counterpart: the
  * reference samples a whole row on one CPU thread). The same result as
  * rsc_shard_partial + an all-gather + rsc_shard_merge, with the all-gather
- * replaced by reads of the other ranks' record arrays in place, over NVLink.
- * Each rank keeps its record array and an array of n_shards ready words in
- * memory that every rank can address (for example a symmetric allocation),
- * and per step:
- *   1. rsc_shard_partial into its own record array;
- *   2. rsc_shard_publish(d_ready_ptrs, n_shards, my_shard, step): after the
- *      stream's earlier work, stores `step` into word my_shard of every rank's
- *      ready array (d_ready_ptrs: a device array of the n_shards ranks' ready
- *      arrays), with a system-wide fence first;
- *   3. rsc_shard_merge_peers(..., d_peer_records, d_ready, step, ...):
- *      d_peer_records is a device array of the n_shards ranks' record arrays
- *      (rank order), d_ready this rank's ready array. The kernel waits until
- *      every rank's word has reached `step` (wrap-around compare), bounded by
- *      the library's 2 s wait limit (rows then report RSC_ROW_INTERNAL), and
- *      merges as rsc_shard_merge.
- * `step` must increase by one per call. A rank rewrites its record array only
- * in its next step's partial pass, which follows its own merge of this step,
- * and every rank's merge of the next step waits for that rank's next
- * publication; two record arrays used alternately (by step parity) therefore
- * keep a slow rank's reads of this step intact. n_shards <= 32 and
- * n_shards * (top_k + RSC_SHARD_TIE_CAP) <= 512, else RSC_ERR_CAPACITY.
+ * replaced by reads of the other ranks' record arrays in place, over NVLink,
+ * and the merge split across the ranks. Every array below lives in memory
+ * that every rank can address (for example a symmetric allocation); pointer
+ * arrays are device arrays of n_shards entries in rank order. Per step, on
+ * every rank:
+ *   1. rsc_shard_partial into this rank's record array;
+ *   2. rsc_shard_publish(ready_records_ptrs, n_shards, my_shard, step): after
+ *      the stream's earlier work, stores `step` into word my_shard of every
+ *      rank's records-ready array, after a system-wide fence;
+ *   3. rsc_shard_merge_peers: waits until every word of this rank's
+ *      records-ready array has reached `step` (wrap-around compare; bounded by
+ *      the library's 2 s wait limit, after which rows report
+ *      RSC_ROW_INTERNAL), merges rows [rows * my_shard / n_shards, rows *
+ *      (my_shard + 1) / n_shards) exactly as rsc_shard_merge, writes their
+ *      results into every rank's result arrays, and stores `step` into word
+ *      my_shard of every rank's results-ready array;
+ *   4. rsc_shard_collect: waits (bounded) until this rank's results-ready
+ *      words have reached `step`, then copies this rank's result arrays into
+ *      the caller's outputs.
+ * With per-row generator states instead of uniforms, every rank merges every
+ * row (d_ready_results_ptrs null; results are not shared; step 4 is skipped and
+ * the outputs are this rank's result arrays), so that every rank advances
+ * every state.
+ * `step` increases by one per call; *d_done_counter (a word of this rank) is
+ * zero before the first call and is left zero. Two record arrays and two sets
+ * of result arrays used alternately (by step parity) keep a slow rank's reads
+ * and writes of one step apart from the next. n_shards <= 32 and n_shards *
+ * (top_k + RSC_SHARD_TIE_CAP) <= 512, else RSC_ERR_CAPACITY.
  */
-RSC_API rsc_status rsc_shard_merge_peers(rsc_sampler *sampler, const void *const *d_peer_records,
-                                         const uint32_t *d_ready, uint32_t step, size_t n_shards,
+typedef struct rsc_peer_exchange {
+    const void *const *d_peer_records;       /* n_shards record arrays ([rows] records each) */
+    const uint32_t *d_ready_records;         /* this rank's records-ready words (n_shards) */
+    uint32_t *const *d_ready_results_ptrs;   /* every rank's results-ready words; null: not shared */
+    uint32_t *d_done_counter;                /* one word of this rank */
+    uint32_t *const *d_peer_ids;             /* every rank's result ids ([rows]) */
+    int32_t *const *d_peer_status;           /* every rank's result statuses */
+    float *const *d_peer_probs;              /* every rank's result probabilities, or null */
+} rsc_peer_exchange;
+
+RSC_API rsc_status rsc_shard_merge_peers(rsc_sampler *sampler, const rsc_peer_exchange *exchange,
+                                         uint32_t step, size_t n_shards, size_t my_shard,
                                          size_t rows, size_t global_vocab,
                                          const rsc_params *params, const float *d_uniforms,
-                                         uint64_t *d_rng_states, uint32_t *d_out_ids,
-                                         int32_t *d_out_status, float *d_out_probs, void *stream);
+                                         uint64_t *d_rng_states, void *stream);
 RSC_API rsc_status rsc_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards,
                                      size_t my_shard, uint32_t step, void *stream);
+RSC_API rsc_status rsc_shard_collect(const uint32_t *d_ready_results, uint32_t step,
+                                     size_t n_shards, size_t rows, const uint32_t *d_ids,
+                                     const int32_t *d_status, const float *d_probs,
+                                     uint32_t *d_out_ids, int32_t *d_out_status,
+                                     float *d_out_probs, void *stream);
 
 /* Number of kernel launches the library issued since the handle was created
  * (for the benchmark's launch count). */

@@ -18,6 +18,18 @@ pub(crate) const RSC_ROW_VOCAB_OVERFLOW: i32 = 2;
 pub(crate) const RSC_ROW_INTERNAL: i32 = 3;
 pub(crate) const RSC_ROW_CODE_MASK: i32 = 0xff;
 
+/// rsc_peer_exchange: device addresses of the arrays the ranks share.
+#[repr(C)]
+pub(crate) struct RscPeerExchange {
+    pub d_peer_records: *const *const c_void,
+    pub d_ready_records: *const u32,
+    pub d_ready_results_ptrs: *const *mut u32,
+    pub d_done_counter: *mut u32,
+    pub d_peer_ids: *const *mut u32,
+    pub d_peer_status: *const *mut i32,
+    pub d_peer_probs: *const *mut f32,
+}
+
 /// `rsc_params`: `SamplingParams` field for field
 /// (crates/rusticide-sampling/src/params.rs:5-12).
 #[repr(C)]
@@ -249,15 +261,25 @@ unsafe extern "C" {
     pub(crate) fn rsc_expf(d_x: *const f32, d_y: *mut f32, n: usize, stream: *mut c_void) -> c_int;
     pub(crate) fn rsc_shard_merge_peers(
         sampler: *mut RscSampler,
-        d_peer_records: *const *const c_void,
-        d_ready: *const u32,
+        exchange: *const RscPeerExchange,
         step: u32,
         n_shards: usize,
+        my_shard: usize,
         rows: usize,
         global_vocab: usize,
         params: *const RscParams,
         d_uniforms: *const f32,
         d_rng_states: *mut u64,
+        stream: *mut c_void,
+    ) -> c_int;
+    pub(crate) fn rsc_shard_collect(
+        d_ready_results: *const u32,
+        step: u32,
+        n_shards: usize,
+        rows: usize,
+        d_ids: *const u32,
+        d_status: *const i32,
+        d_probs: *const f32,
         d_out_ids: *mut u32,
         d_out_status: *mut i32,
         d_out_probs: *mut f32,

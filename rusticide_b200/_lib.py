@@ -47,6 +47,20 @@ class RscParams(ctypes.Structure):
     ]
 
 
+class RscPeerExchange(ctypes.Structure):
+    """rsc_peer_exchange: device addresses of the arrays the ranks share."""
+
+    _fields_ = [
+        ("d_peer_records", ctypes.c_void_p),
+        ("d_ready_records", ctypes.c_void_p),
+        ("d_ready_results_ptrs", ctypes.c_void_p),
+        ("d_done_counter", ctypes.c_void_p),
+        ("d_peer_ids", ctypes.c_void_p),
+        ("d_peer_status", ctypes.c_void_p),
+        ("d_peer_probs", ctypes.c_void_p),
+    ]
+
+
 class RscSampleExtras(ctypes.Structure):
     """rsc_sample_extras."""
 
@@ -84,8 +98,9 @@ SIGNATURES = {
     "rsc_shard_record_bytes": (_SZ, [ctypes.c_uint32]),
     "rsc_shard_partial": (_ST, [_P, _P, _SZ, _SZ, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P]),
     "rsc_shard_merge": (_ST, [_P, _P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P, _P]),
-    "rsc_shard_merge_peers": (_ST, [_P, _P, _P, ctypes.c_uint32, _SZ, _SZ, _SZ,
-                                    ctypes.POINTER(RscParams), _P, _P, _P, _P, _P, _P]),
+    "rsc_shard_merge_peers": (_ST, [_P, ctypes.POINTER(RscPeerExchange), ctypes.c_uint32, _SZ, _SZ,
+                                    _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P]),
+    "rsc_shard_collect": (_ST, [_P, ctypes.c_uint32, _SZ, _SZ, _P, _P, _P, _P, _P, _P, _P]),
     "rsc_shard_publish": (_ST, [_P, _SZ, _SZ, ctypes.c_uint32, _P]),
     "rsc_sample_noalloc": (_ST, [_P, _SZ, _SZ, _SZ, ctypes.POINTER(RscParams), _P, _P, _P, _P, _P,
                                  _P]),

@@ -693,17 +693,16 @@ rsc_status rsc_expf(const float *d_x, float *d_y, size_t n, void *stream) {
     return cuda_status(rsc::launch_expf(d_x, d_y, n, static_cast<cudaStream_t>(stream)));
 }
 
-rsc_status rsc_shard_merge_peers(rsc_sampler *s, const void *const *d_peer_records,
-                                 const uint32_t *d_ready, uint32_t step, size_t n_shards,
-                                 size_t rows, size_t global_vocab, const rsc_params *params,
-                                 const float *d_uniforms, uint64_t *d_rng_states,
-                                 uint32_t *d_out_ids, int32_t *d_out_status, float *d_out_probs,
-                                 void *stream) {
+rsc_status rsc_shard_merge_peers(rsc_sampler *s, const rsc_peer_exchange *x, uint32_t step,
+                                 size_t n_shards, size_t my_shard, size_t rows,
+                                 size_t global_vocab, const rsc_params *params,
+                                 const float *d_uniforms, uint64_t *d_rng_states, void *stream) {
     if (!s || !s->alive) return RSC_ERR_NOT_INITIALIZED;
-    if (!params || n_shards == 0) return RSC_ERR_INVALID_ARGUMENT;
+    if (!params || !x || n_shards == 0 || my_shard >= n_shards) return RSC_ERR_INVALID_ARGUMENT;
     if (global_vocab > kMaxVocab) return RSC_ERR_VOCAB_TOO_LARGE;
     if (rows > s->max_rows) return RSC_ERR_CAPACITY;
-    if (rows > 0 && (!d_peer_records || !d_ready || !d_out_ids || !d_out_status))
+    if (rows > 0 && (!x->d_peer_records || !x->d_ready_records || !x->d_peer_ids ||
+                     !x->d_peer_status || (x->d_ready_results_ptrs && !x->d_done_counter)))
         return RSC_ERR_INVALID_ARGUMENT;
     rsc::CallParams cp = make_params(*params, global_vocab, d_uniforms, d_rng_states);
     if (!cp.topk_active || !cp.normal_scale) return RSC_ERR_INVALID_ARGUMENT;
@@ -711,13 +710,32 @@ rsc_status rsc_shard_merge_peers(rsc_sampler *s, const void *const *d_peer_recor
     const size_t cap = static_cast<size_t>(params->top_k) + RSC_SHARD_TIE_CAP;
     if (n_shards > 32 || n_shards * cap > rsc::kSmallCap) return RSC_ERR_CAPACITY;
     if (!cp.argmax_branch && rows > 0 && !d_uniforms && !d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
+    // Generator states advance on the rank that draws: every rank merges every row.
+    const bool share = x->d_ready_results_ptrs != nullptr;
+    if (share && d_rng_states) return RSC_ERR_INVALID_ARGUMENT;
     if (rows == 0) return RSC_OK;
     DeviceGuard guard(s->device);
-    cudaError_t e = rsc::launch_shard_merge_peers(
-        d_peer_records, d_ready, step, n_shards, rows, rsc::shard_record_bytes(params->top_k), cp,
-        d_out_ids, d_out_status, d_out_probs, static_cast<cudaStream_t>(stream));
+    const size_t r0 = share ? rows * my_shard / n_shards : 0;
+    const size_t r1 = share ? rows * (my_shard + 1) / n_shards : rows;
+    rsc::PeerPointers pp{x->d_peer_records, x->d_ready_records, x->d_ready_results_ptrs,
+                         x->d_done_counter, x->d_peer_ids, x->d_peer_status, x->d_peer_probs};
+    cudaError_t e = rsc::launch_shard_merge_peers(pp, step, n_shards, my_shard, r0, r1,
+                                                  rsc::shard_record_bytes(params->top_k), cp,
+                                                  static_cast<cudaStream_t>(stream));
     ++s->launches;
     return cuda_status(e);
+}
+
+rsc_status rsc_shard_collect(const uint32_t *d_ready_results, uint32_t step, size_t n_shards,
+                             size_t rows, const uint32_t *d_ids, const int32_t *d_status,
+                             const float *d_probs, uint32_t *d_out_ids, int32_t *d_out_status,
+                             float *d_out_probs, void *stream) {
+    if (n_shards == 0 || n_shards > 32) return RSC_ERR_INVALID_ARGUMENT;
+    if (rows > 0 && (!d_ready_results || !d_ids || !d_status || !d_out_ids || !d_out_status))
+        return RSC_ERR_INVALID_ARGUMENT;
+    return cuda_status(rsc::launch_shard_collect(d_ready_results, step, n_shards, rows, d_ids,
+                                                 d_status, d_probs, d_out_ids, d_out_status,
+                                                 d_out_probs, static_cast<cudaStream_t>(stream)));
 }
 
 rsc_status rsc_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards, size_t my_shard,

@@ -151,14 +151,29 @@ cudaError_t launch_shard_partial(const float *logits, size_t rows, uint32_t shar
                                  void *records, size_t rec_bytes, int num_sms,
                                  cudaStream_t stream);
 
-// The merge reading each rank's records in place (peer memory): d_peer_records
-// is a device array of n_shards record-array pointers (n_shards <= 32; one warp
-// merges a row, so n_shards * (k + RSC_SHARD_TIE_CAP) <= kSmallCap), d_ready
-// n_shards words of this GPU that rank p sets to the step it has published.
-cudaError_t launch_shard_merge_peers(const void *const *d_peer_records, const uint32_t *d_ready,
-                                     uint32_t step, size_t n_shards, size_t rows,
-                                     size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
-                                     int32_t *out_status, float *out_probs, cudaStream_t stream);
+// The merge reading each rank's records in place (peer memory; see
+// rsc_peer_exchange in the C header for the pointers): rows [row_begin,
+// row_end) merged here, with n_shards <= 32 and one warp per row (n_shards * (k +
+// RSC_SHARD_TIE_CAP) <= kSmallCap). With ready_results_ptrs set, the results go
+// to every rank's arrays and the last CTA publishes them.
+struct PeerPointers {
+    const void *const *records;
+    const uint32_t *ready_records;
+    uint32_t *const *ready_results_ptrs;
+    uint32_t *done_counter;
+    uint32_t *const *ids;
+    int32_t *const *status;
+    float *const *probs;
+};
+cudaError_t launch_shard_merge_peers(const PeerPointers &x, uint32_t step, size_t n_shards,
+                                     size_t my_shard, size_t row_begin, size_t row_end,
+                                     size_t rec_bytes, const CallParams &p, cudaStream_t stream);
+// Waits (bounded) for every rank's results of `step`, then copies this rank's
+// result arrays to the caller's.
+cudaError_t launch_shard_collect(const uint32_t *ready_results, uint32_t step, size_t n_shards,
+                                 size_t rows, const uint32_t *ids, const int32_t *status,
+                                 const float *probs, uint32_t *out_ids, int32_t *out_status,
+                                 float *out_probs, cudaStream_t stream);
 // Stores `step` into word my_shard of every rank's ready array (d_ready_ptrs: a
 // device array of n_shards pointers, peer memory) after a system-wide fence.
 cudaError_t launch_shard_publish(uint32_t *const *d_ready_ptrs, size_t n_shards, uint32_t my_shard,

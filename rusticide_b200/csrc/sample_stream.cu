@@ -1688,63 +1688,135 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
 }
 
 // The vocab-sharded merge reading every rank's records in place over NVLink
-// (peer memory), instead of from an all-gathered copy: records[p] is rank p's
-// record array ([rows] records, in rank p's memory, mapped here), ready[p] a
-// word in this GPU's memory that rank p sets to the step it has published.
-// Before reading, each CTA waits (bounded) until every ready[p] has reached
+// (peer memory), instead of from an all-gathered copy. x.records[p] is rank
+// p's record array ([rows] records in rank p's memory, mapped here);
+// x.ready_records[p], a word of this GPU, is the step rank p has published.
+// Before reading, each CTA waits (bounded) until every ready word has reached
 // `step`; a wait that runs out marks the CTA's rows RSC_ROW_INTERNAL and reads
-// nothing. The rows then merge exactly as in shard_merge_kernel.
+// nothing. Rows [row_begin, row_end) are merged exactly as in
+// shard_merge_kernel, their results written to this rank's output arrays
+// (x.ids[my_shard], ...) and, when results are shared, to every other rank's
+// too; the last CTA to finish then stores `step` into word my_shard of every
+// rank's results-ready array (x.ready_results_ptrs[p]).
+struct PeerArgs {
+    const unsigned char *const *records;
+    const uint32_t *ready_records;
+    uint32_t *const *ready_results_ptrs;  // null: results are not shared
+    uint32_t *done_counter;
+    uint32_t *const *ids;
+    int32_t *const *status;
+    float *const *probs;  // null: no probabilities
+};
+
+__device__ __forceinline__ bool wait_ready(const uint32_t *ready, uint32_t n, uint32_t step) {
+    const unsigned long long t0 = global_ns();
+    for (uint32_t p = 0; p < n; ++p) {
+        while (true) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ready + p) : "memory");
+            if (static_cast<int32_t>(v - step) >= 0) break;
+            if (global_ns() - t0 > kWaitLimitNs) return false;
+            __nanosleep(200);
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void store_release_sys(uint32_t *dst, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst), "r"(v) : "memory");
+}
+
 __global__ void __launch_bounds__(kMergeWarps * 32)
-shard_merge_peers_kernel(const unsigned char *const *__restrict__ records,
-                         const uint32_t *ready, uint32_t step, uint32_t n_shards, size_t rows,
-                         size_t rec_bytes, const __grid_constant__ CallParams cp,
-                         uint32_t *__restrict__ out_ids, int32_t *__restrict__ out_status,
-                         float *__restrict__ out_probs) {
+shard_merge_peers_kernel(const __grid_constant__ PeerArgs x, uint32_t step, uint32_t n_shards,
+                         uint32_t my_shard, size_t row_begin, size_t row_end, size_t rec_bytes,
+                         const __grid_constant__ CallParams cp) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     MergeSmem &sm = *reinterpret_cast<MergeSmem *>(smem_raw);
     __shared__ uint32_t all_ready;
     __shared__ const unsigned char *base[kMergeMaxPeers];
     load_exp_table(sm.exp_tab);
-    if (threadIdx.x < n_shards) base[threadIdx.x] = records[threadIdx.x];
-    if (threadIdx.x == 0) {
-        bool ok = true;
-        const unsigned long long t0 = global_ns();
-        for (uint32_t p = 0; p < n_shards && ok; ++p) {
-            while (true) {
-                uint32_t v;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ready + p) : "memory");
-                if (static_cast<int32_t>(v - step) >= 0) break;
-                if (global_ns() - t0 > kWaitLimitNs) {
-                    ok = false;
-                    break;
-                }
-                __nanosleep(200);
-            }
-        }
-        all_ready = ok ? 1u : 0u;
-    }
+    if (threadIdx.x < n_shards) base[threadIdx.x] = x.records[threadIdx.x];
+    if (threadIdx.x == 0) all_ready = wait_ready(x.ready_records, n_shards, step) ? 1u : 0u;
     __syncthreads();
+    uint32_t *const ids = x.ids[my_shard];
+    int32_t *const status = x.status[my_shard];
+    float *const probs = x.probs ? x.probs[my_shard] : nullptr;
+    const bool share = x.ready_results_ptrs != nullptr;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     CandList &L = sm.list[warp];
     FinishWork &fw = sm.fw[warp];
-    for (size_t row = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; row < rows;
-         row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
+    for (size_t row = row_begin + static_cast<size_t>(blockIdx.x) * kMergeWarps + warp;
+         row < row_end; row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
         bool ok = all_ready != 0u;
         uint32_t count = 0;
         if (ok)
             count = merge_parts_batched(
                 L, fw, [&](uint32_t part) { return base[part] + row * rec_bytes; }, n_shards,
                 cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
-        if (!ok) {
+        if (ok) {
+            finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, ids, status, probs);
+        } else {
             if (lane == 0) {
-                out_ids[row] = 0;
-                out_status[row] = RSC_ROW_INTERNAL;
-                if (out_probs) out_probs[row] = __uint_as_float(0x7fc00000u);
+                ids[row] = 0;
+                status[row] = RSC_ROW_INTERNAL;
+                if (probs) probs[row] = __uint_as_float(0x7fc00000u);
             }
             __syncwarp();
-            continue;
         }
-        finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+        if (share && lane == 0) {
+            // This row's results to every other rank (NVLink stores).
+            const uint32_t id = ids[row];
+            const int32_t st = status[row];
+            const float pb = probs ? probs[row] : 0.0f;
+            for (uint32_t p = 0; p < n_shards; ++p) {
+                if (p == my_shard) continue;
+                x.ids[p][row] = id;
+                x.status[p][row] = st;
+                if (probs) x.probs[p][row] = pb;
+            }
+        }
+        __syncwarp();
+    }
+    if (share) {
+        // The last CTA to finish publishes the results (every CTA fences its
+        // stores at system scope before it counts itself done).
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            const uint32_t prev = atomicAdd(x.done_counter, 1u);
+            if (prev + 1u == gridDim.x) {
+                __threadfence_system();
+                for (uint32_t p = 0; p < n_shards; ++p)
+                    store_release_sys(x.ready_results_ptrs[p] + my_shard, step);
+                *x.done_counter = 0u;
+            }
+        }
+    }
+}
+
+// The shared results of `step`, once every rank has published them (bounded
+// wait, as above), copied from this rank's result arrays to the caller's; a
+// wait that runs out gives RSC_ROW_INTERNAL rows.
+__global__ void shard_collect_kernel(const uint32_t *ready_results, uint32_t step, uint32_t n_shards,
+                                     size_t rows, const uint32_t *__restrict__ ids,
+                                     const int32_t *__restrict__ status,
+                                     const float *__restrict__ probs, uint32_t *__restrict__ out_ids,
+                                     int32_t *__restrict__ out_status,
+                                     float *__restrict__ out_probs) {
+    __shared__ uint32_t ok;
+    if (threadIdx.x == 0) ok = wait_ready(ready_results, n_shards, step) ? 1u : 0u;
+    __syncthreads();
+    for (size_t r = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < rows;
+         r += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        if (ok) {
+            out_ids[r] = __ldcg(ids + r);
+            out_status[r] = __ldcg(status + r);
+            if (out_probs) out_probs[r] = probs ? __ldcg(probs + r) : __uint_as_float(0x7fc00000u);
+        } else {
+            out_ids[r] = 0;
+            out_status[r] = RSC_ROW_INTERNAL;
+            if (out_probs) out_probs[r] = __uint_as_float(0x7fc00000u);
+        }
     }
 }
 
@@ -2138,20 +2210,39 @@ cudaError_t launch_shard_merge(const void *records, size_t n_shards, size_t rows
 }
 
 
-cudaError_t launch_shard_merge_peers(const void *const *d_peer_records, const uint32_t *d_ready,
-                                     uint32_t step, size_t n_shards, size_t rows,
-                                     size_t rec_bytes, const CallParams &p, uint32_t *out_ids,
-                                     int32_t *out_status, float *out_probs,
-                                     cudaStream_t stream) {
-    if (rows == 0) return cudaSuccess;
-    if (n_shards == 0 || n_shards > kMergeMaxPeers) return cudaErrorInvalidValue;
+cudaError_t launch_shard_merge_peers(const PeerPointers &x, uint32_t step, size_t n_shards,
+                                     size_t my_shard, size_t row_begin, size_t row_end,
+                                     size_t rec_bytes, const CallParams &p, cudaStream_t stream) {
+    if (row_end <= row_begin) {
+        // No rows to merge here; still publish this rank's (empty) share.
+        if (x.ready_results_ptrs) return launch_shard_publish(x.ready_results_ptrs, n_shards,
+                                                               static_cast<uint32_t>(my_shard),
+                                                               step, stream);
+        return cudaSuccess;
+    }
+    if (n_shards == 0 || n_shards > kMergeMaxPeers || my_shard >= n_shards) return cudaErrorInvalidValue;
     cudaError_t e = prepare(shard_merge_peers_kernel, sizeof(MergeSmem));
     if (e != cudaSuccess) return e;
-    const size_t grid = (rows + kMergeWarps - 1) / kMergeWarps;
+    const size_t grid = (row_end - row_begin + kMergeWarps - 1) / kMergeWarps;
+    PeerArgs a{reinterpret_cast<const unsigned char *const *>(x.records), x.ready_records,
+               x.ready_results_ptrs, x.done_counter, x.ids, x.status, x.probs};
     shard_merge_peers_kernel<<<static_cast<unsigned>(grid), kMergeWarps * 32, sizeof(MergeSmem),
-                               stream>>>(
-        reinterpret_cast<const unsigned char *const *>(d_peer_records), d_ready, step,
-        static_cast<uint32_t>(n_shards), rows, rec_bytes, p, out_ids, out_status, out_probs);
+                               stream>>>(a, step, static_cast<uint32_t>(n_shards),
+                                         static_cast<uint32_t>(my_shard), row_begin, row_end,
+                                         rec_bytes, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shard_collect(const uint32_t *ready_results, uint32_t step, size_t n_shards,
+                                 size_t rows, const uint32_t *ids, const int32_t *status,
+                                 const float *probs, uint32_t *out_ids, int32_t *out_status,
+                                 float *out_probs, cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    size_t grid = (rows + 255) / 256;
+    if (grid > 1024) grid = 1024;
+    shard_collect_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+        ready_results, step, static_cast<uint32_t>(n_shards), rows, ids, status, probs, out_ids,
+        out_status, out_probs);
     return cudaGetLastError();
 }
 

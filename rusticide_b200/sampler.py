@@ -354,24 +354,30 @@ class Engine:
                                          int(step) & 0xFFFFFFFF, _stream_ptr(self.device)),
               "rsc_shard_publish")
 
-    def shard_merge_peers(self, peer_records: torch.Tensor, ready: int, step: int, n_shards: int,
-                          rows: int, global_vocab: int, params: SamplingParams,
+    def shard_merge_peers(self, exchange, step: int, n_shards: int, my_shard: int, rows: int,
+                          global_vocab: int, params: SamplingParams,
                           uniforms: Optional[torch.Tensor] = None,
-                          rng_states: Optional[torch.Tensor] = None, want_probs: bool = True,
-                          out=None):
-        """rsc_shard_merge_peers: the merge reading every rank's record array
-        in place (peer_records: int64 device tensor of the ranks' record-array
-        addresses; ready: address of this rank's ready words)."""
+                          rng_states: Optional[torch.Tensor] = None) -> None:
+        """rsc_shard_merge_peers (exchange: an _lib.RscPeerExchange of device
+        addresses); the results land in the exchange's result arrays."""
         self.ensure(rows, 1)
-        ids, status, probs = out if out is not None else self._outputs(rows, want_probs)
         c = params.to_c()
-        check(self.lib.rsc_shard_merge_peers(self._h, peer_records.data_ptr(), int(ready),
-                                             int(step) & 0xFFFFFFFF, int(n_shards), rows,
-                                             int(global_vocab), ctypes.byref(c), _ptr(uniforms),
-                                             _ptr(rng_states), ids.data_ptr(), status.data_ptr(),
-                                             _ptr(probs), _stream_ptr(self.device)),
+        check(self.lib.rsc_shard_merge_peers(self._h, ctypes.byref(exchange), int(step) & 0xFFFFFFFF,
+                                             int(n_shards), int(my_shard), rows, int(global_vocab),
+                                             ctypes.byref(c), _ptr(uniforms), _ptr(rng_states),
+                                             _stream_ptr(self.device)),
               "rsc_shard_merge_peers")
-        return ids, status, probs
+
+    def shard_collect(self, ready_results: int, step: int, n_shards: int, rows: int, ids: int,
+                      status: int, probs: Optional[int], out):
+        """rsc_shard_collect: waits for every rank's results of `step`, then
+        copies this rank's result arrays (device addresses) into `out`."""
+        oi, os_, op = out
+        check(self.lib.rsc_shard_collect(int(ready_results), int(step) & 0xFFFFFFFF, int(n_shards),
+                                         rows, int(ids), int(status), probs, oi.data_ptr(),
+                                         os_.data_ptr(), _ptr(op), _stream_ptr(self.device)),
+              "rsc_shard_collect")
+        return out
 
     def shard_merge(self, gathered: torch.Tensor, n_shards: int, rows: int, global_vocab: int,
                     params: SamplingParams, uniforms: Optional[torch.Tensor] = None,

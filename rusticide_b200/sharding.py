@@ -189,17 +189,23 @@ class VocabShardedSampler:
 
 
 class PeerVocabShardedSampler(VocabShardedSampler):
-    """The vocab-sharded step with the all-gather replaced by reads in place:
-    each rank's records and ready words live in a symmetric allocation (every
-    rank maps every other rank's copy), the partial pass writes this rank's
-    records, rsc_shard_publish tells every rank the step is ready, and
-    rsc_shard_merge_peers reads all ranks' records over NVLink (plain loads)
-    once each rank's ready word for this step has arrived. Two record arrays,
-    used by step parity, keep a slow rank's reads intact (see the C header).
-    The result equals VocabShardedSampler's and the unsharded call's. Needs
-    one warp merge per row: world * (k + 24) <= 512 entries and world <= 32."""
+    """The vocab-sharded step with the all-gather replaced by reads in place
+    and the merge split across the ranks. Every rank's records, result arrays
+    and ready words live in one symmetric allocation (every rank maps every
+    other rank's copy). Per step: the partial pass writes this rank's records;
+    rsc_shard_publish tells every rank they are ready; rsc_shard_merge_peers
+    reads all ranks' records over NVLink (plain loads) for this rank's share of
+    the rows and writes their results into every rank's result arrays;
+    rsc_shard_collect waits for every share and copies the results out. Two
+    record arrays and two result sets, used by step parity, keep consecutive
+    steps apart (see the C header). With generator states instead of
+    uniforms every rank merges every row, so that every rank advances every
+    state. The result equals VocabShardedSampler's and the unsharded call's.
+    Needs one warp merge per row: world * (k + 24) <= 512 and world <= 32."""
 
-    READY_BYTES = 256  # ready words of up to 64 ranks
+    # Byte offsets in the allocation: records-ready words, results-ready
+    # words, the done counter, then the two record arrays and two result sets.
+    READY_RECORDS, READY_RESULTS, COUNTER, HEAD = 0, 256, 512, 768
 
     def __init__(self, engine, vocab: int, group: Optional[dist.ProcessGroup] = None):
         super().__init__(engine, vocab, group)
@@ -210,25 +216,44 @@ class PeerVocabShardedSampler(VocabShardedSampler):
         key = (rows, top_k, str(device))
         if self._peer is None or self._peer["key"] != key:
             import os
-            # Plain peer loads only: no multicast object is needed.
+            # Plain peer loads and stores only: no multicast object is needed.
             os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
             import torch.distributed._symmetric_memory as symm
+            from . import _lib
             rb = self.engine.shard_record_bytes(top_k)
-            span = (rows * rb + 255) // 256 * 256
-            buf = symm.empty(self.READY_BYTES + 2 * span, dtype=torch.uint8, device=device)
+            rec_span = (rows * rb + 255) // 256 * 256
+            col = (rows * 4 + 255) // 256 * 256  # one result column (ids, status or probs)
+            total = self.HEAD + 2 * rec_span + 2 * 3 * col
+            buf = symm.empty(total, dtype=torch.uint8, device=device)
             buf.zero_()
             torch.cuda.synchronize(device)
             handle = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
             ptrs = [int(p) for p in handle.buffer_ptrs]
             if len(ptrs) != self.world:
                 raise RuntimeError(f"symmetric allocation spans {len(ptrs)} ranks, not {self.world}")
-            recs = [torch.tensor([p + self.READY_BYTES + par * span for p in ptrs],
-                                 dtype=torch.int64, device=device) for par in (0, 1)]
-            ready_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=device)
-            # Every rank has zeroed its ready words before any rank publishes.
+
+            def arr(offsets):
+                return torch.tensor(offsets, dtype=torch.int64, device=device)
+
+            res0 = self.HEAD + 2 * rec_span
+            sets = []
+            for par in (0, 1):
+                rbase = self.HEAD + par * rec_span
+                obase = res0 + par * 3 * col
+                sets.append({
+                    "records": arr([p + rbase for p in ptrs]),
+                    "ids": arr([p + obase for p in ptrs]),
+                    "status": arr([p + obase + col for p in ptrs]),
+                    "probs": arr([p + obase + 2 * col for p in ptrs]),
+                    "rec_off": rbase, "out_off": obase,
+                })
+            ready_records_ptrs = arr([p + self.READY_RECORDS for p in ptrs])
+            ready_results_ptrs = arr([p + self.READY_RESULTS for p in ptrs])
+            # Every rank has zeroed its words before any rank publishes.
             dist.barrier(group=self.group)
-            self._peer = {"key": key, "buf": buf, "handle": handle, "recs": recs,
-                          "ready_ptrs": ready_ptrs, "rb": rb, "span": span}
+            self._peer = {"key": key, "buf": buf, "handle": handle, "sets": sets, "rb": rb,
+                          "col": col, "ready_records_ptrs": ready_records_ptrs,
+                          "ready_results_ptrs": ready_results_ptrs, "lib": _lib}
             self._step = 0
         return self._peer
 
@@ -241,11 +266,31 @@ class PeerVocabShardedSampler(VocabShardedSampler):
         st = self._peer_state(rows, params.top_k, logits_shard.device)
         self._step += 1
         step, par = self._step, self._step & 1
-        off = self.READY_BYTES + par * st["span"]
-        mine = st["buf"][off:off + rows * st["rb"]]
+        cur = st["sets"][par]
+        buf, base = st["buf"], st["buf"].data_ptr()
+        mine = buf[cur["rec_off"]:cur["rec_off"] + rows * st["rb"]]
         self.engine.shard_partial(logits_shard, self.offset, self.vocab, params, records=mine)
-        self.engine.shard_publish(st["ready_ptrs"], self.world, self.rank, step)
-        return self.engine.shard_merge_peers(st["recs"][par], st["buf"].data_ptr(), step,
-                                             self.world, rows, self.vocab, params,
-                                             uniforms=uniforms, rng_states=rng_states,
-                                             want_probs=want_probs, out=out)
+        self.engine.shard_publish(st["ready_records_ptrs"], self.world, self.rank, step)
+        share = rng_states is None
+        x = st["lib"].RscPeerExchange(
+            cur["records"].data_ptr(), base + self.READY_RECORDS,
+            st["ready_results_ptrs"].data_ptr() if share else None, base + self.COUNTER,
+            cur["ids"].data_ptr(), cur["status"].data_ptr(),
+            cur["probs"].data_ptr() if want_probs else None)
+        self.engine.shard_merge_peers(x, step, self.world, self.rank, rows, self.vocab, params,
+                                      uniforms=uniforms, rng_states=rng_states)
+        out = out if out is not None else self.engine._outputs(rows, want_probs)
+        ids_addr = base + cur["out_off"]
+        if share:
+            return self.engine.shard_collect(base + self.READY_RESULTS, step, self.world, rows,
+                                             ids_addr, ids_addr + st["col"],
+                                             ids_addr + 2 * st["col"] if want_probs else None, out)
+        # Every row was merged here: this rank's result arrays hold them all.
+        oi, os_, op = out
+        col = st["col"]
+        oi.copy_(buf[cur["out_off"]:cur["out_off"] + rows * 4].view(torch.int32))
+        os_.copy_(buf[cur["out_off"] + col:cur["out_off"] + col + rows * 4].view(torch.int32))
+        if op is not None:
+            op.copy_(buf[cur["out_off"] + 2 * col:cur["out_off"] + 2 * col + rows * 4]
+                     .view(torch.float32))
+        return out

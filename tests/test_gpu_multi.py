@@ -206,6 +206,13 @@ def _rank_peer(rank, world, port, q):
             ids, status, probs = vs.sample(mine, SamplingParams(0.8, 40, 0.95), uniforms=u.to(dev))
             res.append((ids.cpu().numpy().tolist(), status.cpu().numpy().tolist(),
                         probs.cpu().numpy().view(np.uint32).tolist()))
+        # One more step with per-row generator states (every rank merges every row).
+        x, _ = _peer_inputs(PEER_STEPS)
+        mine = x[:, vs.offset:vs.offset + vs.width].contiguous().to(dev)
+        states = engine(rank).rng_seed(torch.arange(PEER_ROWS, dtype=torch.int64, device=dev) + 7)
+        ids, status, probs = vs.sample(mine, SamplingParams(0.8, 40, 0.95), rng_states=states)
+        res.append((ids.cpu().numpy().tolist(), status.cpu().numpy().tolist(),
+                    probs.cpu().numpy().view(np.uint32).tolist(), states.cpu().numpy().tolist()))
         torch.cuda.synchronize(dev)
         dist.barrier()
         q.put((rank, res, None, None))
@@ -230,3 +237,10 @@ def test_peer_memory_vocab_sharded_matches_unsharded():
                 pb.cpu().numpy().view(np.uint32).tolist())
         for r in range(world):
             assert got[r][0][step] == want, f"rank {r} step {step}"
+    x, _ = _peer_inputs(PEER_STEPS)
+    states = engine(0).rng_seed(torch.arange(PEER_ROWS, dtype=torch.int64, device=dev) + 7)
+    ids, st, pb = engine(0).sample(x.to(dev), SamplingParams(0.8, 40, 0.95), rng_states=states)
+    want = (ids.cpu().numpy().tolist(), st.cpu().numpy().tolist(),
+            pb.cpu().numpy().view(np.uint32).tolist(), states.cpu().numpy().tolist())
+    for r in range(world):
+        assert got[r][0][PEER_STEPS] == want, f"rank {r} generator-state step"
