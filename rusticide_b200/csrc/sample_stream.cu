@@ -70,12 +70,33 @@ constexpr uint32_t kMinPartChunks = 16;
 
 // Workspace of one finishing warp.
 struct FinishWork {
+    static constexpr uint32_t kCapacity = kCap;  // survivors it can finish
     unsigned long long items[kCap];   // (~key, idx): value desc, index asc
     unsigned long long items2[kCap];  // (idx, key): index asc
     float vals[kCap];
     uint32_t hist[256];
     uint32_t sel[2];
 };
+
+// The vocab-sharded merge's workspace of one warp: room for kMergeCap
+// survivors of the keep test (k plus ties), in 2.5 KB instead of 11 KB, so
+// that more merging warps fit an SM. The radix select's histogram shares
+// items2's space: finish_list is done with it before items2 is written. A row
+// with more survivors (more than kMergeCap - k values tied with the k-th) is
+// finished again with a FinishWork.
+constexpr uint32_t kMergeCap = 128;
+struct MergeWork {
+    static constexpr uint32_t kCapacity = kMergeCap;
+    unsigned long long items[kMergeCap];
+    union {
+        unsigned long long items2[kMergeCap];
+        uint32_t hist[256];
+    };
+    float vals[kMergeCap];
+    uint32_t sel[2];
+};
+static_assert(sizeof(unsigned long long) * kMergeCap == sizeof(uint32_t) * 256,
+              "the histogram fills items2's space exactly");
 
 struct StreamSmem {
     alignas(128) float ring[kStages][kChunk];
@@ -316,8 +337,8 @@ __device__ __forceinline__ uint32_t pow2_at_least(uint32_t n) {
 
 // Survivors of the keep test against `thr` packed into fw.items (warp ballot
 // compaction); returns their number.
-template <typename Pack>
-__device__ __forceinline__ uint32_t gather_survivors(FinishWork &fw, const uint32_t *ckey,
+template <typename FW, typename Pack>
+__device__ __forceinline__ uint32_t gather_survivors(FW &fw, const uint32_t *ckey,
                                                      const uint32_t *cidx, uint32_t count,
                                                      Pack pack) {
     const int lane = threadIdx.x & 31;
@@ -361,8 +382,12 @@ __device__ __forceinline__ uint32_t precut_list(CandList &L, uint32_t count, flo
     return n;
 }
 
-// Finishes a row from its candidate list (one warp). Writes the row's outputs.
-__device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *ckey,
+// Finishes a row from its candidate list (one warp). Writes the row's outputs
+// and returns true; with a workspace smaller than the list (MergeWork) it
+// returns false, having written nothing, when more candidates survive the
+// keep test than the workspace holds.
+template <typename FW>
+__device__ bool finish_list(FW &fw, const double *tab, const uint32_t *ckey,
                             const uint32_t *cidx, uint32_t count, const CallParams &cp, size_t row,
                             uint32_t *out_ids, int32_t *out_status, float *out_probs) {
     const int lane = threadIdx.x & 31;
@@ -429,6 +454,14 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
             const uint32_t kth = group_select_kth_largest<32, SyncWarp>(
                 count, cp.top_k, [&](uint32_t i) { return ckey[i]; }, fw.hist, fw.sel);
             thr = key_to_float(kth);
+        }
+        if constexpr (FW::kCapacity < kCap) {
+            uint32_t ns = 0;
+            for (uint32_t base = 0; base < count; base += 32) {
+                const uint32_t i = base + lane;
+                ns += __popc(__ballot_sync(0xffffffffu, i < count && survives(key_to_float(ckey[i]), thr)));
+            }
+            if (ns > FW::kCapacity) return false;
         }
         n = gather_survivors(fw, ckey, cidx, count,
                              [&](uint32_t key, uint32_t idx, unsigned long long *it) {
@@ -569,6 +602,7 @@ __device__ void finish_list(FinishWork &fw, const double *tab, const uint32_t *c
         if (out_probs) out_probs[row] = prob;
     }
     __syncwarp();
+    return true;
 }
 
 // Record of one part of a row (a vocab shard, or a segment of a split row),
@@ -731,8 +765,8 @@ __device__ uint32_t merge_records(CandList &L, FinishWork &fw, RecAt rec_at, uin
 // of its entries, so a row costs one or two L2 round trips instead of one per
 // part. The union is the same set of entries (in another order, which the
 // finisher's ranks do not see), cut by the same bound and checked the same way.
-template <typename RecAt>
-__device__ uint32_t merge_parts_batched(CandList &L, FinishWork &fw, RecAt rec_at, uint32_t n,
+template <typename FW, typename RecAt>
+__device__ uint32_t merge_parts_batched(CandList &L, FW &fw, RecAt rec_at, uint32_t n,
                                         uint32_t cap_entries, const CallParams &cp, bool *ok) {
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t flags = 0, ndrop = 0, ncand = 0;
@@ -1647,15 +1681,93 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
 // its candidate list and finishes the row exactly as the streaming kernel does.
 // Two warps per CTA: 31 KB of shared memory a CTA, so 7 CTAs (14 warps) share
 // an SM, against 12 warps with four-warp CTAs.
-constexpr int kMergeWarps = 2;
+constexpr int kMergeWarps = 4;
 // Most ranks the peer-memory merge reads (records in flight per warp).
 constexpr uint32_t kMergeMaxPeers = 32;
 
-struct MergeSmem {
+// Shared memory of a merge CTA. Each warp merges one row with a MergeWork
+// (about 6.5 KB a warp with its list, so eight CTAs, 32 warps, fit an SM).
+// The rare row whose survivors overflow a MergeWork (heavy ties at the k-th
+// value) is merged again after the CTA's rows, by warp 0, with a CandList
+// and a FinishWork laid over the warps' space.
+struct MergeLanes {
     CandList list[kMergeWarps];
-    FinishWork fw[kMergeWarps];
-    double exp_tab[32];
+    MergeWork fw[kMergeWarps];
 };
+struct MergeRetry {
+    CandList list;
+    FinishWork fw;
+};
+struct MergeSmem {
+    double exp_tab[32];
+    uint32_t retry;  // bit w: warp w's row is to be merged again
+    union {
+        MergeLanes lanes;
+        MergeRetry full;
+    };
+};
+static_assert(sizeof(MergeRetry) <= sizeof(MergeLanes), "the retry workspace fits the warps' space");
+
+// Merges one row (one warp): the union of the parts' records, cut by their
+// bounds, finished exactly. Returns false when the workspace is too small
+// for the row's survivors (nothing written then); a union that cannot be
+// trusted is reported as RSC_ROW_INTERNAL.
+template <typename FW, typename RecAt>
+__device__ __forceinline__ bool merge_row(CandList &L, FW &fw, const double *tab, RecAt rec_at,
+                                          uint32_t n_parts, const CallParams &cp, size_t row,
+                                          uint32_t *out_ids, int32_t *out_status,
+                                          float *out_probs) {
+    bool ok = true;
+    const uint32_t count =
+        merge_parts_batched(L, fw, rec_at, n_parts, cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
+    if (!ok) {
+        if ((threadIdx.x & 31) == 0) {
+            out_ids[row] = 0;
+            out_status[row] = RSC_ROW_INTERNAL;
+            if (out_probs) out_probs[row] = __uint_as_float(0x7fc00000u);
+        }
+        __syncwarp();
+        return true;
+    }
+    return finish_list(fw, tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+}
+
+// The rows [r0, r0 + kMergeWarps) of a merge CTA, one per warp (rows past
+// `end` are skipped), then the retries on the full workspace. `done(row)`
+// runs on each warp after its row's outputs are written. Every thread of the
+// CTA calls this.
+template <typename RecAt, typename Done>
+__device__ __forceinline__ void merge_cta_rows(MergeSmem &sm, size_t r0, size_t end,
+                                               RecAt rec_at_row, uint32_t n_parts,
+                                               const CallParams &cp, uint32_t *out_ids,
+                                               int32_t *out_status, float *out_probs, Done done) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) sm.retry = 0;
+    __syncthreads();
+    const size_t row = r0 + warp;
+    if (row < end) {
+        auto rec_at = [&](uint32_t part) { return rec_at_row(part, row); };
+        if (merge_row(sm.lanes.list[warp], sm.lanes.fw[warp], sm.exp_tab, rec_at, n_parts, cp, row,
+                      out_ids, out_status, out_probs)) {
+            done(row);
+        } else if (lane == 0) {
+            atomicOr(&sm.retry, 1u << warp);
+        }
+    }
+    __syncthreads();
+    const uint32_t retry = sm.retry;
+    if (retry != 0u && warp == 0) {
+        for (int w = 0; w < kMergeWarps; ++w) {
+            if (!(retry & (1u << w))) continue;
+            const size_t rr = r0 + w;
+            auto rec_at = [&](uint32_t part) { return rec_at_row(part, rr); };
+            merge_row(sm.full.list, sm.full.fw, sm.exp_tab, rec_at, n_parts, cp, rr, out_ids,
+                      out_status, out_probs);
+            done(rr);
+        }
+    }
+    __syncthreads();
+}
 
 __global__ void __launch_bounds__(kMergeWarps * 32)
 shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, size_t rows,
@@ -1664,26 +1776,12 @@ shard_merge_kernel(const unsigned char *__restrict__ records, size_t n_shards, s
     extern __shared__ __align__(128) unsigned char smem_raw[];
     MergeSmem &sm = *reinterpret_cast<MergeSmem *>(smem_raw);
     load_exp_table(sm.exp_tab);
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    CandList &L = sm.list[warp];
-    FinishWork &fw = sm.fw[warp];
-    for (size_t row = static_cast<size_t>(blockIdx.x) * kMergeWarps + warp; row < rows;
-         row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
-        bool ok = true;
-        const uint32_t count = merge_parts_batched(
-            L, fw, [&](uint32_t part) { return records + (part * rows + row) * rec_bytes; },
-            static_cast<uint32_t>(n_shards), cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
-        if (!ok) {
-            if (lane == 0) {
-                out_ids[row] = 0;
-                out_status[row] = RSC_ROW_INTERNAL;
-                if (out_probs) out_probs[row] = __uint_as_float(0x7fc00000u);
-            }
-            __syncwarp();
-            continue;
-        }
-        finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, out_ids, out_status, out_probs);
+    for (size_t r0 = static_cast<size_t>(blockIdx.x) * kMergeWarps; r0 < rows;
+         r0 += static_cast<size_t>(gridDim.x) * kMergeWarps) {
+        merge_cta_rows(
+            sm, r0, rows,
+            [&](uint32_t part, size_t row) { return records + (part * rows + row) * rec_bytes; },
+            static_cast<uint32_t>(n_shards), cp, out_ids, out_status, out_probs, [](size_t) {});
     }
 }
 
@@ -1743,28 +1841,10 @@ shard_merge_peers_kernel(const __grid_constant__ PeerArgs x, uint32_t step, uint
     float *const probs = x.probs ? x.probs[my_shard] : nullptr;
     const bool share = x.ready_results_ptrs != nullptr;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    CandList &L = sm.list[warp];
-    FinishWork &fw = sm.fw[warp];
-    for (size_t row = row_begin + static_cast<size_t>(blockIdx.x) * kMergeWarps + warp;
-         row < row_end; row += static_cast<size_t>(gridDim.x) * kMergeWarps) {
-        bool ok = all_ready != 0u;
-        uint32_t count = 0;
-        if (ok)
-            count = merge_parts_batched(
-                L, fw, [&](uint32_t part) { return base[part] + row * rec_bytes; }, n_shards,
-                cp.top_k + RSC_SHARD_TIE_CAP, cp, &ok);
-        if (ok) {
-            finish_list(fw, sm.exp_tab, L.key, L.idx, count, cp, row, ids, status, probs);
-        } else {
-            if (lane == 0) {
-                ids[row] = 0;
-                status[row] = RSC_ROW_INTERNAL;
-                if (probs) probs[row] = __uint_as_float(0x7fc00000u);
-            }
-            __syncwarp();
-        }
+    // This row's results to every other rank (NVLink stores), by lane 0 of
+    // the warp that wrote them.
+    auto share_row = [&](size_t row) {
         if (share && lane == 0) {
-            // This row's results to every other rank (NVLink stores).
             const uint32_t id = ids[row];
             const int32_t st = status[row];
             const float pb = probs ? probs[row] : 0.0f;
@@ -1776,6 +1856,26 @@ shard_merge_peers_kernel(const __grid_constant__ PeerArgs x, uint32_t step, uint
             }
         }
         __syncwarp();
+    };
+    for (size_t r0 = row_begin + static_cast<size_t>(blockIdx.x) * kMergeWarps; r0 < row_end;
+         r0 += static_cast<size_t>(gridDim.x) * kMergeWarps) {
+        if (all_ready != 0u) {
+            merge_cta_rows(
+                sm, r0, row_end,
+                [&](uint32_t part, size_t row) { return base[part] + row * rec_bytes; }, n_shards,
+                cp, ids, status, probs, share_row);
+        } else {
+            const size_t row = r0 + warp;
+            if (row < row_end) {
+                if (lane == 0) {
+                    ids[row] = 0;
+                    status[row] = RSC_ROW_INTERNAL;
+                    if (probs) probs[row] = __uint_as_float(0x7fc00000u);
+                }
+                __syncwarp();
+                share_row(row);
+            }
+        }
     }
     if (share) {
         // The last CTA to finish publishes the results (every CTA fences its

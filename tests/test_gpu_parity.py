@@ -394,16 +394,23 @@ def test_vocab_sharded_matches_unsharded(eng, n_shards, top_k):
     = 512 entries per row one warp merges them; beyond (10 and 16 shards at
     k 40, 8 at k 100, 4 at k 128) one block per row does. At k 100 and 128
     some shard rows overflow the streaming list and are rescued into their
-    records by the partial pass's epilogue."""
+    records by the partial pass's epilogue. Row 5 holds up to 40 values tied
+    at its maximum in every shard (480 in all at most, within one finisher's
+    list): from 4 shards on, more survive the keep test than a merging
+    warp's lean workspace holds (128), and the row is merged again with the
+    full one."""
     cfg = synth.CONFIGS["cfg4"]
     rows = 16
     x = synth.make_config(cfg, rows=rows, base_seed=606)
     x[3, 100:140] = 9.0   # ties across a shard boundary
+    V = cfg.vocab
+    bounds = [V * s // n_shards for s in range(n_shards + 1)]
+    ties = min(40, 480 // n_shards)
+    for s in range(n_shards):
+        x[5, bounds[s] + 10:bounds[s] + 10 + ties] = 40.0  # ties at the row's maximum
     u = synth.uniforms(rows, seed=13)
     params = SamplingParams(cfg.temperature, top_k or cfg.top_k, cfg.top_p)
     xd = dev(x)
-    V = cfg.vocab
-    bounds = [V * s // n_shards for s in range(n_shards + 1)]
     recs = []
     for s in range(n_shards):
         shard = xd[:, bounds[s]:bounds[s + 1]]
