@@ -133,3 +133,37 @@ def test_lmhead_partial_shards_merge_to_the_fused_call(eng, rows, dim, vocab, n_
     assert torch.equal(ids_m, ids_f)
     assert torch.equal(pr_m.view(torch.int32), pr_f.view(torch.int32))
     assert (st_m & 0xFF).eq(0).all()
+
+
+@pytest.mark.parametrize("rows", [64, 256])
+def test_lmhead_qwen_shape(eng, rows):
+    """The Qwen2.5 LM head at full size, vocab 151936 x dim 4096 (the product
+    crates/rusticide-transformer/src/decoder.rs:104-105 forms), through both
+    kernels (up to 64 rows the swapped-operand one, above it the row-tile
+    one): the logits are within the f32 bound of the product, the fused call
+    equals rsc_sample on them bit for bit, and 16 rows match the oracle."""
+    dim, vocab = 4096, 151936
+    h, w = _inputs(rows, dim, vocab, seed=rows + 4096)
+    params = SamplingParams(0.8, 40, 0.95)
+    g = torch.Generator(device="cuda").manual_seed(rows)
+    u = torch.rand(rows, device="cuda", generator=g)
+    ids_f, st_f, pr_f = eng.lmhead_sample(h, w, params, uniforms=u)
+    logits = eng.lmhead_logits(h, w)
+    ids_s, st_s, pr_s = eng.sample(logits, params, uniforms=u)
+    torch.cuda.synchronize()
+    assert torch.equal(st_f, st_s)
+    assert torch.equal(ids_f, ids_s)
+    assert torch.equal(pr_f.view(torch.int32), pr_s.view(torch.int32))
+    assert (st_f & 0xFF).eq(0).all()
+
+    hf = h.float()
+    for c0 in range(0, vocab, 32768):
+        wf = w[c0:c0 + 32768].float()
+        want = hf @ wf.T
+        bound = 2.0 * dim * 2.0 ** -24 * (hf.abs() @ wf.abs().T) + 1e-30
+        assert ((logits[:, c0:c0 + 32768] - want).abs() <= bound).all(), f"columns from {c0}"
+
+    from oracle import oracle as O
+    x = logits[:16].cpu().numpy()
+    ref = O.sample_rows(x, O.params(0.8, 40, 0.95), u[:16].cpu().numpy(), threads=4)
+    assert np.array_equal(ids_f[:16].cpu().numpy().astype(np.int64), ref["token"].astype(np.int64))
