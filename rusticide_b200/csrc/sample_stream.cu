@@ -1281,6 +1281,28 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                         }
                     }
                     lmax = fmaxf(lmax, __fmul_rn(cmr, scale));
+                    if constexpr (kRecord) {
+                        // A vocab shard's rows are a few chunks long, and the
+                        // first chunks' bound admits about 1% of each: the
+                        // lane maxima of the second chunk too (its stage is
+                        // peeked, not consumed) halve what the first two admit.
+                        if (c + 1 < c1) {
+                            const uint32_t s2 = (consumed + 1u) % kStages;
+                            got &= mbar_wait(&sm.full[s2], ((consumed + 1u) / kStages) & 1u);
+                            const uint32_t len2 = min(kChunk, g.nbody - (c + 1u) * kChunk);
+                            const float4 *r42 = reinterpret_cast<const float4 *>(sm.ring[s2]);
+                            float cm2 = kNegInf;
+#pragma unroll
+                            for (uint32_t jj = 0; jj < kChunk / 4 / kConsumers; ++jj) {
+                                const uint32_t q = threadIdx.x + jj * kConsumers;
+                                if (4 * q < len2) {
+                                    const float4 f = r42[q];
+                                    cm2 = fmaxf(fmaxf(cm2, fmaxf(f.x, f.y)), fmaxf(f.z, f.w));
+                                }
+                            }
+                            lmax = fmaxf(lmax, __fmul_rn(cm2, scale));
+                        }
+                    }
                     post_warp_bound(sm, lmax, t_bound, cw, par);
                     if (consumers_any(!got)) {
                         stop = true;
