@@ -67,6 +67,10 @@ constexpr uint32_t kNoList = 0xffffffffu;
 // Shortest row part the balanced schedule makes for batches of at most one
 // row per CTA.
 constexpr uint32_t kMinPartChunks = 16;
+// Chunks past a piece's first whose lane maxima join its first bound (the
+// ring holds them all: the first chunk and kPeekChunks more).
+constexpr uint32_t kPeekChunks = 2;
+static_assert(kPeekChunks < kStages, "the peeked chunks and the first fit the ring");
 
 // Workspace of one finishing warp.
 struct FinishWork {
@@ -1281,15 +1285,18 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                         }
                     }
                     lmax = fmaxf(lmax, __fmul_rn(cmr, scale));
-                    if constexpr (kRecord) {
-                        // A vocab shard's rows are a few chunks long, and the
-                        // first chunks' bound admits about 1% of each: the
-                        // lane maxima of the second chunk too (its stage is
-                        // peeked, not consumed) halve what the first two admit.
-                        if (c + 1 < c1) {
-                            const uint32_t s2 = (consumed + 1u) % kStages;
-                            got &= mbar_wait(&sm.full[s2], ((consumed + 1u) / kStages) & 1u);
-                            const uint32_t len2 = min(kChunk, g.nbody - (c + 1u) * kChunk);
+                    // A bound from one chunk admits about 1% of each chunk
+                    // until the first refresh; with the lane maxima of the
+                    // next kPeekChunks chunks too (their stages are peeked,
+                    // not consumed: the producer is at most kStages ahead)
+                    // the first chunks admit about a third of that. This
+                    // matters most on a vocab shard's rows, a few chunks long.
+#pragma unroll
+                    for (uint32_t e = 1; e <= kPeekChunks; ++e) {
+                        if (c + e < c1) {
+                            const uint32_t s2 = (consumed + e) % kStages;
+                            got &= mbar_wait(&sm.full[s2], ((consumed + e) / kStages) & 1u);
+                            const uint32_t len2 = min(kChunk, g.nbody - (c + e) * kChunk);
                             const float4 *r42 = reinterpret_cast<const float4 *>(sm.ring[s2]);
                             float cm2 = kNegInf;
 #pragma unroll
