@@ -1390,12 +1390,12 @@ stream_topk_kernel(const float *__restrict__ logits, size_t rows, uint32_t vocab
                     }
                 }
                 const bool last = c + 1 == c1;
-                // Bounds refresh after chunks 2, 4, 8, then every 8, and at the
-                // end; for k above 64 also after each of the first 4 chunks: the
-                // first chunks' bound is then loose enough to fill the list
-                // before the second chunk ends.
+                // Bounds refresh after chunks 4 and 8, then every 8, and at the
+                // end. (After chunks 1 to kPeekChunks + 1 a refresh would add
+                // nothing: the first bound already holds their lane maxima.)
                 const uint32_t done = c + 1 - c0;
-                const bool refresh = last || (done < 8 ? (done & (done - 1)) == 0 && done > 1 : done % 8 == 0);
+                const bool refresh =
+                    last || (done < 8 ? (done & (done - 1)) == 0 && done > kPeekChunks + 1 : done % 8 == 0);
                 if (!refresh) continue;
                 if (t_bound) post_warp_bound(sm, lmax, t_bound, cw, par);
                 // One barrier per refresh: settles the list, publishes
